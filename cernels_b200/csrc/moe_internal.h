@@ -1,0 +1,103 @@
+// Internal (not exported) declarations shared between the kernel translation
+// units and the C-ABI layer: the workspace layout and the kernel launchers.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <cstddef>
+#include <cstdint>
+
+#include "../../include/cernels_b200.h"
+
+namespace cernels {
+
+// Routing works on chunks of kRouteChunk flat (token, slot) entries per CTA.
+constexpr int kRouteChunk = 1024;
+constexpr int kRouteThreads = 256;
+constexpr int kMaxExperts = 2048;
+
+// Grouped-GEMM tile shape (rows of the permuted token matrix per tile).
+constexpr int kBlockM = 128;
+
+// Decode path limits: total (token, slot) pairs per call.
+constexpr int kDecodeMaxPairs = 1024;
+
+inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+// Device pointers carved out of one caller-provided workspace allocation.
+struct PrefillWorkspace {
+  int* status;          // [1] device status word (cernels::DeviceStatus)
+  int* block_counts;    // [n_chunks * E] per-chunk histograms, then per-chunk bases
+  int* offsets;         // [E + 1] row offset of each expert in the permuted order
+  int* mtile_offsets;   // [E + 1] cumulative count of 128-row tiles per expert
+  int* perm_flat;       // [Tk] flat (token * topk + slot) index of each permuted row
+  int* perm_token;      // [Tk] token id of each permuted row
+  float* perm_weight;   // [Tk] router weight of each permuted row
+  int* inv;             // [Tk] permuted row of each flat entry (-1 when skipped)
+  __nv_bfloat16* gathered;  // [Tk, H] token rows in permuted (expert-major) order
+  __nv_bfloat16* glu;       // [Tk, F] activation output of the gate/up GEMM
+  __nv_bfloat16* down_out;  // [Tk, H] output of the down GEMM (unweighted)
+};
+
+struct DecodeWorkspace {
+  int* status;       // [1]
+  int* counters;     // [max(H, F) / 8 + 1] arrival counters of the down stage
+  float* glu;        // [Tk, F] fp32 activation rows (flat (token, slot) order)
+  float* partial;    // [Tk, H] fp32 per-pair down-projection rows
+};
+
+size_t prefill_workspace_bytes(const cernels_moe_shape& s);
+PrefillWorkspace carve_prefill_workspace(const cernels_moe_shape& s, void* base);
+size_t decode_workspace_bytes(const cernels_moe_shape& s);
+DecodeWorkspace carve_decode_workspace(const cernels_moe_shape& s, void* base);
+
+// ---- launchers (return cudaError_t of the launch)
+cudaError_t launch_route(const int32_t* indices, const float* weights, int tokens, int topk, int experts,
+                         const PrefillWorkspace& ws, cudaStream_t stream);
+// Copies rows [0, rows) (and only those below *row_count when row_count is non-null).
+cudaError_t launch_gather(const __nv_bfloat16* x, const int* perm_token, int rows, const int* row_count,
+                          int hidden, __nv_bfloat16* gathered, cudaStream_t stream);
+cudaError_t launch_combine(const __nv_bfloat16* down_out, const int* inv, const float* weights, int tokens,
+                           int topk, int hidden, __nv_bfloat16* out, cudaStream_t stream);
+
+struct GroupedGemmArgs {
+  const __nv_bfloat16* a;      // [rows, K] permuted activations
+  const __nv_bfloat16* b;      // expert weights (layout per mode)
+  const float* bias;           // [E, N] fp32 or nullptr
+  __nv_bfloat16* out;          // [rows, out_cols]
+  const int* offsets;          // [E + 1]
+  const int* mtile_offsets;    // [E + 1]
+  int* status;
+  int rows;                    // Tk (row count of a / out)
+  int experts;
+  int k;                       // reduction length
+  int n;                       // columns of the weight product (2F or H)
+  int out_cols;                // F for gate/up, H for down
+};
+
+enum GemmMode : int {
+  kGateUpLinear = 0,   // B = gate_up_proj [E, 2F, H] (K-major), chunked gate|up, SiLU
+  kGateUpGptOss = 1,   // B = gate_up_proj [E, H, 2F] (N-major), interleaved, clamped SwiGLU + bias
+  kDownLinear = 2,     // B = down_proj [E, H, F] (K-major)
+  kDownGptOss = 3,     // B = down_proj [E, F, H] (N-major), + bias
+};
+
+cudaError_t launch_grouped_gemm(GemmMode mode, const GroupedGemmArgs& args, int num_sms, cudaStream_t stream);
+
+struct DecodeArgs {
+  const __nv_bfloat16* x;
+  const __nv_bfloat16* w1;
+  const float* b1;
+  const __nv_bfloat16* w2;
+  const float* b2;
+  const int32_t* indices;
+  const float* weights;
+  __nv_bfloat16* out;
+  int tokens, hidden, experts, inter, topk, layout;
+};
+cudaError_t launch_decode(const DecodeArgs& a, const DecodeWorkspace& ws, cudaStream_t stream);
+
+int device_sm_count();
+
+}  // namespace cernels

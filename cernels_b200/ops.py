@@ -1,0 +1,260 @@
+"""torch.library operators with the reference schemas, implemented over the C ABI.
+
+Each op keeps the schema of the reference's kernel-builder binding, e.g.
+``cohere2_moe_experts(Tensor x, Tensor gate_up_proj, Tensor down_proj, Tensor indices,
+Tensor weights, int topk) -> Tensor`` (src/kops/cohere2_moe_experts/torch-ext/torch_binding.cpp:7-12),
+registered here under the ``cernels_b200`` namespace for CUDA (and Meta, for shape
+propagation). The CUDA implementation runs on the current stream of x's device, takes
+scratch from torch's caching allocator and launches through ctypes; it never
+synchronises, so calls can be captured in CUDA graphs.
+
+Errors mirror the reference's TORCH_CHECKs: wrong dtype, device, rank or contiguity
+raise RuntimeError before any launch; expert ids outside [0, E) are skipped silently
+(src/kops/cohere2_moe_experts/csrc/cohere2_moe_experts.cu:35,49-50).
+"""
+
+from __future__ import annotations
+
+import ctypes
+
+import torch
+
+from . import _lib
+
+_NS = "cernels_b200"
+_defined = False
+_LIBS: list = []  # keep torch.library.Library objects alive
+
+SCHEMA_PLAIN = "(Tensor x, Tensor gate_up_proj, Tensor down_proj, Tensor indices, Tensor weights, int topk) -> Tensor"
+SCHEMA_GPTOSS = (
+    "(Tensor x, Tensor gate_up_proj, Tensor gate_up_bias, Tensor down_proj, Tensor down_bias, "
+    "Tensor indices, Tensor weights, int topk) -> Tensor"
+)
+
+# Reference op name -> (schema, layout, decode)
+OPS = {
+    "cohere2_moe_experts": (SCHEMA_PLAIN, _lib.LAYOUT_LINEAR, False),
+    "cohere2_moe_experts_decode": (SCHEMA_PLAIN, _lib.LAYOUT_LINEAR, True),
+    "deepseek_ocr2_moe_experts": (SCHEMA_PLAIN, _lib.LAYOUT_LINEAR, False),
+    "deepseek_ocr2_moe_experts_decode": (SCHEMA_PLAIN, _lib.LAYOUT_LINEAR, True),
+    "qwen3_next_moe_experts": (SCHEMA_PLAIN, _lib.LAYOUT_LINEAR, False),
+    "qwen3_next_moe_experts_decode": (SCHEMA_PLAIN, _lib.LAYOUT_LINEAR, True),
+    "gpt_oss_moe_experts": (SCHEMA_GPTOSS, _lib.LAYOUT_GPTOSS, False),
+    "gpt_oss_moe_experts_decode": (SCHEMA_GPTOSS, _lib.LAYOUT_GPTOSS, True),
+}
+
+DECODE_MAX_PAIRS = 1024
+
+
+def _check(cond: bool, msg: str) -> None:
+    if not cond:
+        raise RuntimeError(msg)
+
+
+def _ptr(t: torch.Tensor | None) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def _stream_handle(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def shape_of(x: torch.Tensor, gate_up_proj: torch.Tensor, down_proj: torch.Tensor, topk: int, layout: int) -> _lib.MoeShape:
+    T, H = x.shape
+    E = gate_up_proj.shape[0]
+    if layout == _lib.LAYOUT_LINEAR:
+        F = gate_up_proj.shape[1] // 2
+    else:
+        F = gate_up_proj.shape[2] // 2
+    return _lib.MoeShape(int(T), int(H), int(E), int(F), int(topk), int(layout))
+
+
+def validate(x, gate_up_proj, down_proj, indices, weights, topk, layout, b1=None, b2=None) -> None:
+    """The reference's TORCH_CHECKs plus the dtype / rank checks its kernels assume."""
+    tensors = [("x", x), ("gate_up_proj", gate_up_proj), ("down_proj", down_proj), ("indices", indices),
+               ("weights", weights)]
+    if b1 is not None:
+        tensors.append(("gate_up_bias", b1))
+    if b2 is not None:
+        tensors.append(("down_bias", b2))
+    for name, t in tensors:
+        _check(t.is_cuda, f"{name} must be a CUDA tensor")
+        _check(t.device == x.device, f"{name} must be on {x.device}")
+        _check(t.is_contiguous(), f"{name} must be contiguous")
+    _check(x.dim() == 2 and x.dtype == torch.bfloat16, "x must be [T, H] bf16")
+    _check(gate_up_proj.dim() == 3 and gate_up_proj.dtype == torch.bfloat16, "gate_up_proj must be 3-D bf16")
+    _check(down_proj.dim() == 3 and down_proj.dtype == torch.bfloat16, "down_proj must be 3-D bf16")
+    _check(indices.dtype == torch.int32, "indices must be int32")
+    _check(weights.dtype == torch.float32, "weights must be fp32")
+    T, H = x.shape
+    E = gate_up_proj.shape[0]
+    _check(indices.dim() == 2 and tuple(indices.shape) == (T, topk), "indices must be [T, topk]")
+    _check(weights.dim() == 2 and tuple(weights.shape) == (T, topk), "weights must be [T, topk]")
+    if layout == _lib.LAYOUT_LINEAR:
+        _check(gate_up_proj.shape[2] == H and gate_up_proj.shape[1] % 2 == 0, "gate_up_proj must be [E, 2F, H]")
+        F = gate_up_proj.shape[1] // 2
+        _check(tuple(down_proj.shape) == (E, H, F), "down_proj must be [E, H, F]")
+    else:
+        _check(gate_up_proj.shape[1] == H and gate_up_proj.shape[2] % 2 == 0, "gate_up_proj must be [E, H, 2F]")
+        F = gate_up_proj.shape[2] // 2
+        _check(tuple(down_proj.shape) == (E, F, H), "down_proj must be [E, F, H]")
+        if b1 is not None:
+            _check(b1.dtype == torch.float32 and tuple(b1.shape) == (E, 2 * F), "gate_up_bias must be [E, 2F] fp32")
+        if b2 is not None:
+            _check(b2.dtype == torch.float32 and tuple(b2.shape) == (E, H), "down_bias must be [E, H] fp32")
+    _check(H % 8 == 0 and F % 8 == 0, "H and F must be multiples of 8")
+
+
+def run_experts(x, gate_up_proj, down_proj, indices, weights, topk, layout, decode, b1=None, b2=None,
+                out: torch.Tensor | None = None) -> torch.Tensor:
+    """Validates, allocates output + workspace, and calls the C ABI on x's current stream."""
+    validate(x, gate_up_proj, down_proj, indices, weights, topk, layout, b1, b2)
+    shape = shape_of(x, gate_up_proj, down_proj, topk, layout)
+    if decode and shape.tokens * shape.topk > DECODE_MAX_PAIRS:
+        decode = False  # the grouped-GEMM path covers any size, on the GPU
+    if out is None:
+        out = torch.empty_like(x)
+    if shape.tokens == 0:
+        return out
+    lib = _lib.load()
+    ws_bytes = _lib.workspace_bytes(shape, decode)
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=x.device)
+    fn = lib.cernels_moe_experts_decode if decode else lib.cernels_moe_experts
+    with torch.cuda.device(x.device):
+        rc = fn(ctypes.byref(shape), x.data_ptr(), gate_up_proj.data_ptr(), _ptr(b1), down_proj.data_ptr(), _ptr(b2),
+                indices.data_ptr(), weights.data_ptr(), out.data_ptr(), ws.data_ptr(), ws_bytes,
+                _stream_handle(x.device))
+    _lib.check(rc, "cernels_moe_experts_decode" if decode else "cernels_moe_experts")
+    return out
+
+
+def _make_impl(layout: int, decode: bool, has_bias: bool):
+    if has_bias:
+        def impl(x, gate_up_proj, gate_up_bias, down_proj, down_bias, indices, weights, topk):
+            return run_experts(x, gate_up_proj, down_proj, indices, weights, topk, layout, decode,
+                               gate_up_bias, down_bias)
+    else:
+        def impl(x, gate_up_proj, down_proj, indices, weights, topk):
+            return run_experts(x, gate_up_proj, down_proj, indices, weights, topk, layout, decode)
+    return impl
+
+
+def _meta_impl(has_bias: bool):
+    if has_bias:
+        def meta(x, gate_up_proj, gate_up_bias, down_proj, down_bias, indices, weights, topk):
+            return torch.empty_like(x)
+    else:
+        def meta(x, gate_up_proj, down_proj, indices, weights, topk):
+            return torch.empty_like(x)
+    return meta
+
+
+def register() -> None:
+    """Defines the ``cernels_b200::*`` operators (idempotent)."""
+    global _defined
+    if _defined:
+        return
+    lib_def = torch.library.Library(_NS, "DEF")
+    lib_cuda = torch.library.Library(_NS, "IMPL", "CUDA")
+    lib_meta = torch.library.Library(_NS, "IMPL", "Meta")
+    for name, (schema, layout, decode) in OPS.items():
+        has_bias = schema is SCHEMA_GPTOSS
+        lib_def.define(name + schema)
+        lib_cuda.impl(name, _make_impl(layout, decode, has_bias))
+        lib_meta.impl(name, _meta_impl(has_bias))
+    _LIBS.extend([lib_def, lib_cuda, lib_meta])
+    _defined = True
+
+
+register()
+ops = getattr(torch.ops, _NS)
+
+
+# Python re-exports with the reference's function names
+# (src/kops/cohere2_moe_experts/torch-ext/cohere2_moe_experts/__init__.py:1-12).
+def cohere2_moe_experts(x, gate_up_proj, down_proj, indices, weights, topk):
+    return ops.cohere2_moe_experts(x, gate_up_proj, down_proj, indices, weights, topk)
+
+
+def cohere2_moe_experts_decode(x, gate_up_proj, down_proj, indices, weights, topk):
+    return ops.cohere2_moe_experts_decode(x, gate_up_proj, down_proj, indices, weights, topk)
+
+
+def deepseek_ocr2_moe_experts(x, gate_up_proj, down_proj, indices, weights, topk):
+    return ops.deepseek_ocr2_moe_experts(x, gate_up_proj, down_proj, indices, weights, topk)
+
+
+def deepseek_ocr2_moe_experts_decode(x, gate_up_proj, down_proj, indices, weights, topk):
+    return ops.deepseek_ocr2_moe_experts_decode(x, gate_up_proj, down_proj, indices, weights, topk)
+
+
+def qwen3_next_moe_experts(x, gate_up_proj, down_proj, indices, weights, topk):
+    return ops.qwen3_next_moe_experts(x, gate_up_proj, down_proj, indices, weights, topk)
+
+
+def qwen3_next_moe_experts_decode(x, gate_up_proj, down_proj, indices, weights, topk):
+    return ops.qwen3_next_moe_experts_decode(x, gate_up_proj, down_proj, indices, weights, topk)
+
+
+def gpt_oss_moe_experts(x, gate_up_proj, gate_up_bias, down_proj, down_bias, indices, weights, topk):
+    return ops.gpt_oss_moe_experts(x, gate_up_proj, gate_up_bias, down_proj, down_bias, indices, weights, topk)
+
+
+def gpt_oss_moe_experts_decode(x, gate_up_proj, gate_up_bias, down_proj, down_bias, indices, weights, topk):
+    return ops.gpt_oss_moe_experts_decode(x, gate_up_proj, gate_up_bias, down_proj, down_bias, indices, weights, topk)
+
+
+# ---------------------------------------------------------------- stage entry points
+def route(indices: torch.Tensor, weights: torch.Tensor, experts: int):
+    """Routing only: returns (offsets [E+1], perm_token [Tk], perm_weight [Tk], inv [Tk]).
+
+    Stable in the flat index t*topk+j; ids outside [0, E) are skipped (inv = -1).
+    """
+    _check(indices.is_cuda and indices.dtype == torch.int32 and indices.is_contiguous() and indices.dim() == 2,
+           "indices must be a contiguous [T, topk] int32 CUDA tensor")
+    _check(weights.dtype == torch.float32 and weights.shape == indices.shape and weights.is_contiguous(),
+           "weights must be contiguous fp32 [T, topk]")
+    T, k = indices.shape
+    dev = indices.device
+    shape = _lib.MoeShape(int(T), 8, int(experts), 8, int(k), _lib.LAYOUT_LINEAR)
+    offsets = torch.empty(experts + 1, dtype=torch.int32, device=dev)
+    perm_token = torch.zeros(T * k, dtype=torch.int32, device=dev)
+    perm_weight = torch.zeros(T * k, dtype=torch.float32, device=dev)
+    inv = torch.empty(T * k, dtype=torch.int32, device=dev)
+    ws_bytes = _lib.workspace_bytes(shape, False)
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
+    with torch.cuda.device(dev):
+        rc = _lib.load().cernels_moe_route(ctypes.byref(shape), indices.data_ptr(), weights.data_ptr(),
+                                           offsets.data_ptr(), perm_token.data_ptr(), perm_weight.data_ptr(),
+                                           inv.data_ptr(), ws.data_ptr(), ws_bytes, _stream_handle(dev))
+    _lib.check(rc, "cernels_moe_route")
+    return offsets, perm_token, perm_weight, inv
+
+
+def gather_rows(x: torch.Tensor, perm_token: torch.Tensor, rows: int | None = None) -> torch.Tensor:
+    """rows_out[i] = x[perm_token[i]] for i < rows (bf16 [rows, H])."""
+    _check(x.is_cuda and x.dtype == torch.bfloat16 and x.is_contiguous() and x.dim() == 2, "x must be [T, H] bf16")
+    _check(perm_token.dtype == torch.int32 and perm_token.is_contiguous(), "perm_token must be int32")
+    n = perm_token.numel() if rows is None else int(rows)
+    out = torch.empty(n, x.shape[1], dtype=x.dtype, device=x.device)
+    with torch.cuda.device(x.device):
+        rc = _lib.load().cernels_moe_gather(x.data_ptr(), perm_token.data_ptr(), n, x.shape[1], out.data_ptr(),
+                                            _stream_handle(x.device))
+    _lib.check(rc, "cernels_moe_gather")
+    return out
+
+
+def combine_rows(rows: torch.Tensor, inv: torch.Tensor, weights: torch.Tensor, out: torch.Tensor | None = None):
+    """out[t] = bf16(sum_j weights[t, j] * rows[inv[t*topk + j]]) in fp32, slot order."""
+    T, k = weights.shape
+    H = rows.shape[1]
+    _check(rows.dtype == torch.bfloat16 and rows.is_contiguous(), "rows must be contiguous bf16")
+    _check(inv.dtype == torch.int32 and inv.numel() == T * k, "inv must be int32 [T*topk]")
+    _check(weights.dtype == torch.float32 and weights.is_contiguous(), "weights must be fp32")
+    if out is None:
+        out = torch.empty(T, H, dtype=torch.bfloat16, device=rows.device)
+    with torch.cuda.device(rows.device):
+        rc = _lib.load().cernels_moe_combine(rows.data_ptr(), inv.data_ptr(), weights.data_ptr(), T, k, H,
+                                             out.data_ptr(), _stream_handle(rows.device))
+    _lib.check(rc, "cernels_moe_combine")
+    return out

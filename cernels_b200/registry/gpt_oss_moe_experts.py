@@ -1,0 +1,48 @@
+"""gpt_oss_moe_experts loader — drop-in for src/kops/registry/gpt_oss_moe_experts.py.
+
+``kernel(x, mlp)`` takes hidden states [B, S, H] and a GptOssMLP. The router (linear +
+bias, top-k, softmax over the k logits) runs in torch in the timed path, as in the
+reference loader; the CUDA op does routing, both grouped GEMMs (with biases) and the
+clamped interleaved SwiGLU. Weights are consumed in place in the transformers layout
+([E, H, 2F] interleaved gate/up, [E, F, H]); only the fp32 bias casts are cached on the
+module, as the reference does (its ``_kops_weights``).
+"""
+
+import torch
+
+from .. import ops
+from ._common import module_cache, routing_tensors
+
+
+def _weights(experts):
+    gb, db = experts.gate_up_proj_bias, experts.down_proj_bias
+    stamp = (gb.data_ptr(), gb._version, db.data_ptr(), db._version)
+    b1, b2 = module_cache(experts, "bias_f32", stamp,
+                          lambda: (gb.data.float().contiguous(), db.data.float().contiguous()))
+    return experts.gate_up_proj.data.contiguous(), b1, experts.down_proj.data.contiguous(), b2
+
+
+def kernel(x, mlp):
+    if mlp is None:
+        raise RuntimeError("mlp module not available (meta device)")
+    bsz, seqlen, hidden = x.shape
+    xf = x.reshape(-1, hidden).contiguous()
+    with torch.no_grad():
+        _logits, scores, indices = mlp.router(xf)
+        w1, b1, w2, b2 = _weights(mlp.experts)
+        idx, w = routing_tensors(indices, scores)
+        out = ops.gpt_oss_moe_experts(xf, w1, b1, w2, b2, idx, w, int(mlp.router.top_k))
+    return out.reshape(bsz, seqlen, hidden)
+
+
+def decode_kernel(x, mlp):
+    if mlp is None:
+        raise RuntimeError("mlp module not available (meta device)")
+    bsz, seqlen, hidden = x.shape
+    xf = x.reshape(-1, hidden).contiguous()
+    with torch.no_grad():
+        _logits, scores, indices = mlp.router(xf)
+        w1, b1, w2, b2 = _weights(mlp.experts)
+        idx, w = routing_tensors(indices, scores)
+        out = ops.gpt_oss_moe_experts_decode(xf, w1, b1, w2, b2, idx, w, int(mlp.router.top_k))
+    return out.reshape(bsz, seqlen, hidden)

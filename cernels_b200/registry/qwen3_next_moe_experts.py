@@ -1,0 +1,69 @@
+"""qwen3_next_moe_experts loader — drop-in for src/kops/registry/qwen3_next_moe_experts.py.
+
+``kernel(x, block)`` takes the raw hidden states [B, S, H] and a
+Qwen3NextSparseMoeBlock. As in the reference loader, the router (block.gate: linear +
+fp32 softmax + top-k + renorm) runs in torch in the timed path; the routed experts run in
+the CUDA op; the always-on shared expert ``sigmoid(shared_expert_gate(x)) *
+shared_expert(x)`` runs through the same CUDA grouped-GEMM path as a one-expert,
+one-slot problem whose router weight is the sigmoid gate (its gate/up weights are
+concatenated once into the [1, 2Fs, H] layout and cached on the block).
+"""
+
+import torch
+
+from .. import ops
+from ._common import module_cache, routing_tensors
+
+
+def _shared_weights(block):
+    se = block.shared_expert
+
+    g, u, d = se.gate_proj.weight, se.up_proj.weight, se.down_proj.weight
+    stamp = (g.data_ptr(), g._version, u.data_ptr(), u._version, d.data_ptr(), d._version)
+
+    def build():
+        w1 = torch.cat([g.data, u.data], dim=0).unsqueeze(0).contiguous()  # [1, 2Fs, H]
+        w2 = d.data.unsqueeze(0).contiguous()                               # [1, H, Fs]
+        return w1, w2
+
+    return module_cache(block, "shared", stamp, build)
+
+
+def shared_expert(xf: torch.Tensor, block) -> torch.Tensor:
+    """sigmoid(x @ g^T) * shared_mlp(x) via the CUDA op (one expert, topk = 1)."""
+    w1, w2 = _shared_weights(block)
+    T = xf.shape[0]
+    gate = torch.sigmoid(torch.nn.functional.linear(xf, block.shared_expert_gate.weight).float()).contiguous()
+    idx = torch.zeros(T, 1, dtype=torch.int32, device=xf.device)
+    return ops.qwen3_next_moe_experts(xf, w1, w2, idx, gate, 1)
+
+
+def kernel(x, block):
+    if block is None:
+        raise RuntimeError("block module not available (meta device)")
+    bsz, seqlen, hidden = x.shape
+    xf = x.reshape(-1, hidden).contiguous()
+    with torch.no_grad():
+        _logits, scores, indices = block.gate(xf)
+        e = block.experts
+        idx, w = routing_tensors(indices, scores)
+        routed = ops.qwen3_next_moe_experts(xf, e.gate_up_proj.data.contiguous(), e.down_proj.data.contiguous(),
+                                            idx, w, int(block.gate.top_k))
+        out = routed + shared_expert(xf, block)
+    return out.reshape(bsz, seqlen, hidden)
+
+
+def decode_kernel(x, block):
+    """Decode-shape variant (a few tokens): routed experts through the gather-GEMV path."""
+    if block is None:
+        raise RuntimeError("block module not available (meta device)")
+    bsz, seqlen, hidden = x.shape
+    xf = x.reshape(-1, hidden).contiguous()
+    with torch.no_grad():
+        _logits, scores, indices = block.gate(xf)
+        e = block.experts
+        idx, w = routing_tensors(indices, scores)
+        routed = ops.qwen3_next_moe_experts_decode(xf, e.gate_up_proj.data.contiguous(),
+                                                   e.down_proj.data.contiguous(), idx, w, int(block.gate.top_k))
+        out = routed + shared_expert(xf, block)
+    return out.reshape(bsz, seqlen, hidden)

@@ -1,0 +1,121 @@
+/*
+ * cernels_b200 — C ABI of the B200 (sm_100a) mixture-of-experts "experts" operators.
+ *
+ * Every entry point takes plain device pointers, sizes and a CUDA stream (passed as
+ * void*), launches asynchronously on that stream and returns 0 or a CERNELS_E_* code.
+ * Nothing here allocates device memory: scratch comes from a caller-provided workspace
+ * whose size cernels_moe_workspace_bytes() reports. No entry point synchronises the
+ * stream or reads device memory on the host, so a call can be captured in a CUDA graph.
+ *
+ * Tensor conventions (all contiguous, row-major):
+ *   x              [T, H]        bf16
+ *   gate_up_proj   CERNELS_LAYOUT_LINEAR: [E, 2F, H] bf16  (F.linear layout, rows 0..F-1 gate, F..2F-1 up)
+ *                  CERNELS_LAYOUT_GPTOSS: [E, H, 2F] bf16  (columns interleaved: even gate, odd up)
+ *   gate_up_bias   [E, 2F] fp32, GPTOSS only (may be NULL)
+ *   down_proj      CERNELS_LAYOUT_LINEAR: [E, H, F] bf16;  CERNELS_LAYOUT_GPTOSS: [E, F, H] bf16
+ *   down_bias      [E, H] fp32, GPTOSS only (may be NULL)
+ *   indices        [T, topk] int32 expert id per (token, slot); ids outside [0, E) are skipped
+ *   weights        [T, topk] fp32 router weight per (token, slot)
+ *   out            [T, H] bf16 (fully overwritten)
+ *
+ * Activation: LINEAR  glu = silu(gate) * up
+ *             GPTOSS  g = min(gate, 7), u = clamp(up, -7, 7), glu = (u + 1) * g * sigmoid(1.702 g)
+ * Output:     out[t] = sum_j weights[t, j] * (glu_j @ down[e_j] (+ down_bias[e_j]))   (fp32 accumulate)
+ */
+#ifndef CERNELS_B200_H_
+#define CERNELS_B200_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define CERNELS_LAYOUT_LINEAR 0
+#define CERNELS_LAYOUT_GPTOSS 1
+
+/* Return codes (mirroring the reference's TORCH_CHECK failures, as integers). */
+#define CERNELS_OK 0
+#define CERNELS_E_INVALID_SHAPE 1     /* non-positive or unsupported dimension            */
+#define CERNELS_E_ALIGNMENT 2         /* H or F not a multiple of 8, or pointer misaligned */
+#define CERNELS_E_WORKSPACE 3         /* workspace NULL or smaller than required          */
+#define CERNELS_E_CUDA 4              /* a CUDA runtime / driver call failed              */
+#define CERNELS_E_UNSUPPORTED 5       /* no sm_100 device, or a limit of this build       */
+#define CERNELS_E_NULL 6              /* a required pointer is NULL                       */
+
+typedef struct cernels_moe_shape {
+  int32_t tokens;       /* T */
+  int32_t hidden;       /* H */
+  int32_t experts;      /* E */
+  int32_t intermediate; /* F (per-expert moe_intermediate_size) */
+  int32_t topk;         /* k */
+  int32_t layout;       /* CERNELS_LAYOUT_* */
+} cernels_moe_shape;
+
+/* Human-readable text for a return code (static storage). */
+const char* cernels_error_string(int code);
+
+/* Library version as MAJOR*10000 + MINOR*100 + PATCH. */
+int cernels_version(void);
+
+/* Workspace bytes needed by cernels_moe_experts (decode == 0) or
+ * cernels_moe_experts_decode (decode != 0) for this shape. */
+int cernels_moe_workspace_bytes(const cernels_moe_shape* shape, int decode, size_t* bytes);
+
+/* Prefill / general path: routing -> gather -> tcgen05 grouped GEMM (gate/up + fused
+ * activation) -> tcgen05 grouped GEMM (down) -> deterministic weighted combine.
+ * Replaces the host functions `cohere2_moe_experts`
+ * (src/kops/cohere2_moe_experts/csrc/cohere2_moe_experts.cu:238),
+ * `deepseek_ocr2_moe_experts` (src/kops/deepseek_ocr2_moe_experts/csrc/deepseek_ocr2_moe_experts.cu:240),
+ * `qwen3_next_moe_experts` (src/kops/qwen3_next_moe_experts/csrc/qwen3_next_moe_experts.cu:97) and
+ * `gpt_oss_moe_experts` (src/kops/gpt_oss_moe_experts/csrc/gpt_oss_moe_experts.cu:119). */
+int cernels_moe_experts(const cernels_moe_shape* shape, const void* x, const void* gate_up_proj,
+                        const float* gate_up_bias, const void* down_proj, const float* down_bias,
+                        const int32_t* indices, const float* weights, void* out, void* workspace,
+                        size_t workspace_bytes, void* stream);
+
+/* Decode path (T * topk <= 1024): fused gather-GEMV that streams each selected expert's
+ * weights once, deduplicated across tokens. Replaces `cohere2_moe_experts_decode`
+ * (src/kops/cohere2_moe_experts/csrc/cohere2_moe_experts.cu:199) and
+ * `deepseek_ocr2_moe_experts_decode` (src/kops/deepseek_ocr2_moe_experts/csrc/deepseek_ocr2_moe_experts.cu:201). */
+int cernels_moe_experts_decode(const cernels_moe_shape* shape, const void* x, const void* gate_up_proj,
+                               const float* gate_up_bias, const void* down_proj, const float* down_bias,
+                               const int32_t* indices, const float* weights, void* out, void* workspace,
+                               size_t workspace_bytes, void* stream);
+
+/* ---- Stage entry points (used by the expert-parallel host path and by tests). ---- */
+
+/* Routing: per-expert histogram, offsets[E+1], and a permutation that is stable in the
+ * flat index t*topk+j. Replaces count_tokens_kernel + at::cumsum + build_perm_kernel
+ * (src/kops/cohere2_moe_experts/csrc/cohere2_moe_experts.cu:29-55,259-280).
+ * Outputs (device, caller-allocated): offsets [E+1], perm_token [T*topk],
+ * perm_weight [T*topk], inv [T*topk] (permuted row of each flat entry, -1 if skipped).
+ * Entries past offsets[E] in perm_* are left untouched. */
+int cernels_moe_route(const cernels_moe_shape* shape, const int32_t* indices, const float* weights,
+                      int32_t* offsets, int32_t* perm_token, float* perm_weight, int32_t* inv,
+                      void* workspace, size_t workspace_bytes, void* stream);
+
+/* Gather: rows_out[i, :] = x[perm_token[i], :] for i < rows ([rows, H] bf16). Replaces
+ * gather_kernel (src/kops/cohere2_moe_experts/csrc/cohere2_moe_experts.cu:58-65). Used by
+ * expert parallelism to build the dispatch send buffer in routed order. */
+int cernels_moe_gather(const void* x, const int32_t* perm_token, int32_t rows, int32_t hidden, void* rows_out,
+                       void* stream);
+
+/* Weighted combine: out[t, :] = bf16( sum_j weights[t, j] * rows[inv[t*topk+j], :] ), fp32
+ * accumulation in fixed slot order j = 0..topk-1, entries with inv < 0 skipped. Replaces
+ * scatter_add_f32_kernel + the fp32->bf16 cast
+ * (src/kops/cohere2_moe_experts/csrc/cohere2_moe_experts.cu:85-94,360), deterministically. */
+int cernels_moe_combine(const void* rows, const int32_t* inv, const float* weights, int32_t tokens,
+                        int32_t topk, int32_t hidden, void* out, void* stream);
+
+/* Device status word of the last call that used this workspace (0 = ok; nonzero when a
+ * bounded wait inside a kernel gave up). Reads device memory: synchronises `stream`. */
+int cernels_workspace_status(const cernels_moe_shape* shape, int decode, const void* workspace, int* status,
+                             void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* CERNELS_B200_H_ */

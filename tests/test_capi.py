@@ -1,0 +1,113 @@
+"""CPU: the C-ABI library loads, exports every function declared in include/*.h, and
+rejects invalid arguments with the documented codes (no GPU work is issued)."""
+
+import ctypes
+import re
+from pathlib import Path
+
+import pytest
+import torch
+
+from cernels_b200 import _lib
+
+ROOT = Path(__file__).resolve().parent.parent
+
+
+def declared_functions():
+    names = []
+    for h in sorted((ROOT / "include").glob("*.h")):
+        text = re.sub(r"/\*.*?\*/", "", h.read_text(), flags=re.S)
+        names += re.findall(r"^\s*(?:const\s+)?\w+\s*\*?\s*(cernels_\w+)\s*\(", text, flags=re.M)
+    return names
+
+
+def test_library_exports_every_declared_symbol():
+    lib = _lib.load()
+    names = declared_functions()
+    assert len(names) >= 9
+    for n in names:
+        assert hasattr(lib, n), n
+        assert n in _lib.PROTOTYPES, f"{n} has no ctypes prototype"
+
+
+def test_version_and_error_strings():
+    lib = _lib.load()
+    assert lib.cernels_version() >= 100
+    for code in range(7):
+        assert lib.cernels_error_string(code)
+    assert lib.cernels_error_string(99) == b"unknown error"
+
+
+def shape(T=8, H=64, E=4, F=32, k=2, layout=0):
+    return _lib.MoeShape(T, H, E, F, k, layout)
+
+
+def test_workspace_sizes_grow_with_tokens():
+    a = _lib.workspace_bytes(shape(T=8), False)
+    b = _lib.workspace_bytes(shape(T=800), False)
+    assert 0 < a < b
+    assert _lib.workspace_bytes(shape(T=8), True) > 0
+
+
+@pytest.mark.parametrize("bad,code", [
+    (dict(H=60), 2), (dict(F=12), 2), (dict(E=0), 1), (dict(k=0), 1), (dict(T=-1), 1), (dict(layout=7), 1),
+    (dict(E=4096), 5),
+])
+def test_invalid_shapes_rejected(bad, code):
+    lib = _lib.load()
+    s = shape(**bad)
+    n = ctypes.c_size_t(0)
+    assert lib.cernels_moe_workspace_bytes(ctypes.byref(s), 0, ctypes.byref(n)) == code
+
+
+def test_null_and_workspace_errors_before_any_launch():
+    lib = _lib.load()
+    s = shape()
+    # NULL inputs
+    rc = lib.cernels_moe_experts(ctypes.byref(s), None, None, None, None, None, None, None, None, None, 0, None)
+    assert rc == 6
+    # workspace too small (non-null, aligned fake pointers; rejected before touching them)
+    p = 1 << 20
+    rc = lib.cernels_moe_experts(ctypes.byref(s), p, p, None, p, None, p, p, p, p, 16, None)
+    assert rc == 3
+    # misaligned x
+    rc = lib.cernels_moe_experts(ctypes.byref(s), p + 2, p, None, p, None, p, p, p, p, 1 << 30, None)
+    assert rc == 2
+    # decode pair limit
+    big = shape(T=600, k=2)
+    rc = lib.cernels_moe_experts_decode(ctypes.byref(big), p, p, None, p, None, p, p, p, p, 1 << 40, None)
+    assert rc == 5
+    assert lib.cernels_moe_gather(p, p, 4, 12, p, None) == 2
+    assert lib.cernels_moe_combine(p, p, p, 4, 0, 64, p, None) == 1
+
+
+def test_empty_token_batch_is_a_noop():
+    lib = _lib.load()
+    s = shape(T=0)
+    assert lib.cernels_moe_experts(ctypes.byref(s), None, None, None, None, None, None, None, None, None, 0, None) == 0
+
+
+def test_torch_shim_rejects_cpu_tensors_like_torch_check():
+    from cernels_b200 import ops
+    x = torch.zeros(4, 64, dtype=torch.bfloat16)
+    w1 = torch.zeros(2, 64, 64, dtype=torch.bfloat16)
+    w2 = torch.zeros(2, 64, 32, dtype=torch.bfloat16)
+    idx = torch.zeros(4, 1, dtype=torch.int32)
+    w = torch.zeros(4, 1)
+    with pytest.raises(RuntimeError, match="CUDA"):
+        ops.run_experts(x, w1, w2, idx, w, 1, 0, False)
+
+
+def test_torch_ops_registered_with_reference_schemas():
+    from cernels_b200 import ops
+    for name in ["cohere2_moe_experts", "cohere2_moe_experts_decode", "deepseek_ocr2_moe_experts",
+                 "deepseek_ocr2_moe_experts_decode", "qwen3_next_moe_experts", "gpt_oss_moe_experts"]:
+        schema = str(getattr(torch.ops.cernels_b200, name).default._schema)
+        assert "int topk" in schema and schema.endswith("-> Tensor")
+    # meta propagation works without a GPU
+    x = torch.empty(5, 64, dtype=torch.bfloat16, device="meta")
+    out = torch.ops.cernels_b200.cohere2_moe_experts(
+        x, torch.empty(2, 64, 64, dtype=torch.bfloat16, device="meta"),
+        torch.empty(2, 64, 32, dtype=torch.bfloat16, device="meta"),
+        torch.empty(5, 1, dtype=torch.int32, device="meta"), torch.empty(5, 1, device="meta"), 1)
+    assert out.shape == (5, 64)
