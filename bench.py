@@ -1,0 +1,488 @@
+"""Benchmark of the MoE-experts hot path (one JSON line on rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config NAME] [--impl ours|reference]
+
+A "step" is one call of the reference benchmark's timed operation on one batch:
+  * experts configs (deepseek_v2_lite, qwen3_30b_a3b, decode): the op on (x, top_k_index,
+    top_k_weights, experts) — the reference's ``kernel(x, idx, w, experts)``;
+  * qwen3_next: ``kernel(x, block)`` — router + routed experts + gated shared expert;
+  * gpt_oss_20b (default): ``kernel(x, mlp)`` — router + routed experts with biases.
+``value`` is tokens/s over the whole job with inputs resident in HBM (CUDA events on the
+launch stream, L2 flushed with a 256 MB write before every timed step, max over ranks);
+``e2e`` is the same metric through the same public API from pinned host buffers
+(host->device copy of the step's inputs and device->host copy of its output inside the
+timed region). Multi-GPU runs (torchrun, one rank per GPU) use expert parallelism for
+the EP configs (qwen3_next, gpt_oss_20b): tokens and experts sharded contiguously, NCCL
+all-to-all dispatch/combine; total tokens fixed ("strong" scaling).
+
+``--impl reference`` times the reference's own CPU path — the transformers op_eager
+module the reference benchmarks against — on a bounded token sample on this host's cores.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+if ROOT not in sys.path:
+    sys.path.insert(0, ROOT)
+
+DEFAULT_CONFIG = "gpt_oss_20b"
+EP_CONFIGS = ("qwen3_next", "gpt_oss_20b")
+L2_FLUSH_BYTES = 256 << 20
+
+
+def parse_args(argv=None):
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=20)
+    p.add_argument("--warmup", type=int, default=5)
+    p.add_argument("--config", default=DEFAULT_CONFIG)
+    p.add_argument("--tokens", type=int, default=None, help="override T of the config")
+    p.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    p.add_argument("--cpu-sample-s", type=float, default=15.0, help="target seconds of the CPU baseline sample")
+    p.add_argument("--no-cpu-baseline", action="store_true")
+    p.add_argument("--graph", action="store_true", help="replay the step as a CUDA graph (decode)")
+    return p.parse_args(argv)
+
+
+# ---------------------------------------------------------------- distributed plumbing
+def dist_env():
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return rank, world, local
+
+
+def init_dist(world: int, backend: str):
+    import torch.distributed as dist
+
+    if world > 1 and not dist.is_initialized():
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        dist.init_process_group(backend=backend)
+    return dist
+
+
+# ---------------------------------------------------------------- clocks
+class ClockSampler:
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.path = os.path.join(ROOT, "gpurun_out", f"clocks_rank{gpu_index}.csv")
+
+    def __enter__(self):
+        try:
+            os.makedirs(os.path.dirname(self.path), exist_ok=True)
+            self.fh = open(self.path, "w")
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.QUERY}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=self.fh, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+            self.fh.close()
+
+    def summary(self):
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        rows = []
+        with open(self.path) as f:
+            for line in f:
+                parts = [s.strip() for s in line.split(",")]
+                if len(parts) < 9:
+                    continue
+                try:
+                    rows.append((float(parts[1]), float(parts[2]), float(parts[3]), parts[4:]))
+                except ValueError:
+                    continue
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        loaded = [r for r in rows if r[2] > 300.0] or rows
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in loaded for i, v in enumerate(r[3][1:5]) if v.lower() == "active"})
+        return {"sm_mhz": statistics.median(r[0] for r in loaded), "sm_max_mhz": max(r[1] for r in rows),
+                "reasons": reasons, "samples": len(loaded)}
+
+
+# ---------------------------------------------------------------- workload
+def build_workload(args, device, rank, world):
+    import torch
+
+    from cernels_b200.configs import CONFIGS, make_case
+    from cernels_b200.hf_modules import build_module
+
+    cfg = CONFIGS[args.config]
+    if args.tokens:
+        cfg = cfg.with_tokens(args.tokens)
+    case = make_case(cfg, device=device)
+    kind, module = build_module(case, device=device)
+    return cfg, case, kind, module
+
+
+def make_step(cfg, case, kind, module, world, rank):
+    """Returns (step(x) -> out, input tensors of one step, launches per step)."""
+    import torch
+
+    from cernels_b200.registry import cohere2_moe_experts as c2
+    from cernels_b200.registry import gpt_oss_moe_experts as go
+    from cernels_b200.registry import qwen3_next_moe_experts as qn
+
+    decode = cfg.name == "decode"
+    if world > 1 and cfg.name in EP_CONFIGS:
+        from cernels_b200 import ep
+
+        planner = ep.ExpertParallelMoe.from_module(kind, module, rank, world)
+        shard = ep.token_shard(cfg.tokens, rank, world)
+        x = case.x[shard].contiguous()
+        return (lambda xx: planner.forward(xx)), [x], planner.launches_per_step
+    if kind == "gpt_oss":
+        return (lambda xx: go.kernel(xx.unsqueeze(0), module).squeeze(0)), [case.x], 7
+    if kind == "qwen3_next":
+        return (lambda xx: qn.kernel(xx.unsqueeze(0), module).squeeze(0)), [case.x], 14
+    idx, w = case.indices, case.weights.to(torch.bfloat16)
+    fn = c2.decode_kernel if decode else c2.kernel
+    return (lambda xx, ii, ww: fn(xx, ii, ww, module)), [case.x, idx, w], (2 if decode else 7)
+
+
+def time_device(step, inputs, steps, warmup, flush, graph=False):
+    import torch
+
+    stream = torch.cuda.current_stream()
+    for _ in range(warmup):
+        step(*inputs)
+    torch.cuda.synchronize()
+    g = None
+    if graph:
+        s = torch.cuda.Stream()
+        s.wait_stream(stream)
+        with torch.cuda.stream(s):
+            step(*inputs)
+        stream.wait_stream(s)
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            step(*inputs)
+        torch.cuda.synchronize()
+    total_ms = 0.0
+    per = []
+    for _ in range(steps):
+        flush.zero_()
+        a = torch.cuda.Event(enable_timing=True)
+        b = torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        if g is not None:
+            g.replay()
+        else:
+            step(*inputs)
+        b.record(stream)
+        b.synchronize()
+        ms = a.elapsed_time(b)
+        per.append(ms)
+        total_ms += ms
+    return total_ms, per
+
+
+def time_e2e(step, inputs, steps, warmup, flush):
+    """Pinned host inputs -> device -> step -> host output, per step, CUDA events."""
+    import torch
+
+    stream = torch.cuda.current_stream()
+    host_in = [t.cpu().pin_memory() for t in inputs]
+    dev_in = [torch.empty_like(t) for t in inputs]
+    out_sample = step(*inputs)
+    host_out = torch.empty(out_sample.shape, dtype=out_sample.dtype, pin_memory=True)
+    h2d = sum(t.numel() * t.element_size() for t in host_in)
+    d2h = host_out.numel() * host_out.element_size()
+
+    def one():
+        for d, h in zip(dev_in, host_in):
+            d.copy_(h, non_blocking=True)
+        out = step(*dev_in)
+        host_out.copy_(out, non_blocking=True)
+
+    for _ in range(warmup):
+        one()
+    torch.cuda.synchronize()
+    total = 0.0
+    for _ in range(steps):
+        flush.zero_()
+        a = torch.cuda.Event(enable_timing=True)
+        b = torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        one()
+        b.record(stream)
+        b.synchronize()
+        total += a.elapsed_time(b)
+    return total, h2d, d2h
+
+
+def stage_profile(case, steps):
+    """Per-stage device times (ms) of the experts op via the C-ABI profiling entry."""
+    import ctypes
+
+    import torch
+
+    from cernels_b200 import _lib, ops
+
+    cfg = case.cfg
+    idx = case.indices.to(torch.int32).contiguous()
+    w = case.weights.float().contiguous()
+    shape = ops.shape_of(case.x, case.w1, case.w2, cfg.topk, cfg.layout)
+    nbytes = _lib.workspace_bytes(shape, False)
+    ws = torch.empty(nbytes, dtype=torch.uint8, device=case.x.device)
+    out = torch.empty_like(case.x)
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=case.x.device)
+    acc = [0.0] * 5
+    stage = (ctypes.c_float * 5)()
+    n = 0
+    for i in range(steps + 2):
+        flush.zero_()
+        rc = _lib.load().cernels_moe_experts_profiled(
+            ctypes.byref(shape), case.x.data_ptr(), case.w1.data_ptr(), ops._ptr(case.b1), case.w2.data_ptr(),
+            ops._ptr(case.b2), idx.data_ptr(), w.data_ptr(), out.data_ptr(), ws.data_ptr(), nbytes,
+            torch.cuda.current_stream().cuda_stream, stage)
+        _lib.check(rc, "cernels_moe_experts_profiled")
+        if i >= 2:
+            for j in range(5):
+                acc[j] += stage[j]
+            n += 1
+    return [a / n for a in acc]
+
+
+def load_peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    try:
+        with open(path) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), float(p["bf16_tflops"]), "measured"
+    except Exception:
+        return 6650.0, 1590.0, "fallback"
+
+
+def roofline(cfg, case, stage_ms):
+    """Dominant kernel's achieved rate vs the measured peak."""
+    from cernels_b200.configs import LAYOUT_GPTOSS, touched_experts
+
+    hbm, tflops, src = load_peaks()
+    T, H, F, k = cfg.tokens, cfg.hidden, cfg.inter, cfg.topk
+    tk = T * k
+    e = touched_experts(case.indices, cfg.experts)
+    names = ["route", "gather", "gate_up_gemm", "down_gemm", "combine"]
+    dom = max(range(5), key=lambda i: stage_ms[i])
+    if dom == 3:
+        flops = 2.0 * tk * F * H
+        bytes_ = e * H * F * 2 + tk * F * 2 + tk * H * 2 + (e * H * 4 if cfg.layout == LAYOUT_GPTOSS else 0)
+    else:
+        flops = 4.0 * tk * H * F
+        bytes_ = e * 2 * F * H * 2 + tk * H * 2 + tk * F * 2 + (e * 2 * F * 4 if cfg.layout == LAYOUT_GPTOSS else 0)
+    if dom not in (2, 3):
+        flops = 0.0
+        bytes_ = {0: tk * 8 * 3, 1: tk * H * 4, 4: tk * H * 2 + T * H * 2}[dom]
+    sec = stage_ms[dom] / 1e3
+    intensity = flops / bytes_ if bytes_ else 0.0
+    ridge = tflops * 1e12 / (hbm * 1e9)
+    if flops and intensity >= ridge:
+        achieved = flops / sec / 1e12
+        r = {"bound": "tensor", "achieved": round(achieved, 1), "peak": tflops, "unit": "TFLOP/s"}
+    else:
+        achieved = bytes_ / sec / 1e9
+        r = {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s"}
+    r["frac"] = round(achieved / r["peak"], 4)
+    r["kernel"] = names[dom]
+    r["peak_source"] = src
+    r["traffic"] = None
+    r["stage_ms"] = {n: round(v, 4) for n, v in zip(names, stage_ms)}
+    r["algorithmic"] = {"flops": flops, "bytes": bytes_}
+    return r
+
+
+# ---------------------------------------------------------------- CPU baselines
+def cpu_oracle_baseline(case, target_s):
+    """numpy oracle (oracle/moe_oracle.py, a port of the reference algorithm) on a token sample."""
+    import numpy as np
+
+    from oracle import moe_oracle as O
+
+    cfg = case.cfg
+    x = case.x.float().cpu().numpy()
+    w1 = case.w1.float().cpu().numpy()
+    w2 = case.w2.float().cpu().numpy()
+    b1 = None if case.b1 is None else case.b1.cpu().numpy()
+    b2 = None if case.b2 is None else case.b2.cpu().numpy()
+    idx = case.indices.cpu().numpy()
+    wts = case.weights.float().cpu().numpy()
+    n = min(cfg.tokens, 64)
+    while True:
+        t0 = time.perf_counter()
+        O.moe_experts(x[:n], w1, w2, idx[:n], wts[:n], cfg.layout, b1, b2)
+        dt = time.perf_counter() - t0
+        if dt * 4 > target_s or n >= cfg.tokens:
+            break
+        n = min(cfg.tokens, n * 4)
+    return {"value": round(n / dt, 2), "unit": "tokens/s", "cores": _threads(), "kind": "port",
+            "sample": f"numpy fp32 oracle, first {n} of {cfg.tokens} tokens, 1 call, {dt:.2f} s"}
+
+
+def _threads():
+    import torch
+
+    return int(torch.get_num_threads())
+
+
+def run_reference(args):
+    """The reference's op_eager module (transformers, bf16) on this host's CPU cores."""
+    import torch
+
+    rank, world, _ = dist_env()
+    if rank != 0:
+        return 0
+    torch.set_num_threads(os.cpu_count() or 1)
+    from cernels_b200.configs import CONFIGS, make_case
+    from cernels_b200.hf_modules import build_module, reference_forward
+
+    cfg = CONFIGS[args.config]
+    if args.tokens:
+        cfg = cfg.with_tokens(args.tokens)
+    case = make_case(cfg, device="cpu")
+    kind, module = build_module(case, device="cpu")
+    # bounded sample: grow the token count until one call takes ~target/ (steps)
+    per_step = max(0.5, args.cpu_sample_s / max(1, args.steps + args.warmup))
+    n = min(cfg.tokens, 16)
+    while True:
+        xs = case.x[:n]
+        t0 = time.perf_counter()
+        reference_forward(kind, module, case, xs, case.indices[:n], case.weights[:n])
+        dt = time.perf_counter() - t0
+        if dt * 2 > per_step or n >= cfg.tokens:
+            break
+        n = min(cfg.tokens, n * 2)
+    xs = case.x[:n]
+    for _ in range(args.warmup):
+        reference_forward(kind, module, case, xs, case.indices[:n], case.weights[:n])
+    total = 0.0
+    for _ in range(args.steps):
+        t0 = time.perf_counter()
+        reference_forward(kind, module, case, xs, case.indices[:n], case.weights[:n])
+        total += time.perf_counter() - t0
+    value = n * args.steps / total
+    line = {
+        "impl": "reference", "metric": "MoE-experts tokens/s", "value": round(value, 2), "unit": "tokens/s",
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(total / args.steps * 1e3, 3), "higher_is_better": True,
+        "scaling": "strong" if cfg.name in EP_CONFIGS else "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded, reference config distributions)",
+        "config": {"workload": cfg.name, "tokens": cfg.tokens, "hidden": cfg.hidden, "experts": cfg.experts,
+                   "intermediate": cfg.inter, "topk": cfg.topk, "reference_op": f"transformers {type(module).__name__}"},
+        "cpu_baseline": {"value": round(value, 2), "unit": "tokens/s", "cores": _threads(), "kind": "reference",
+                         "sample": f"first {n} of {cfg.tokens} tokens per step, transformers {type(module).__name__} "
+                                   f"bf16 eager on CPU"},
+        "e2e": {"value": round(value, 2), "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+# ---------------------------------------------------------------- our arm
+def run_ours(args):
+    import torch
+
+    rank, world, local = dist_env()
+    if world != args.gpus:
+        args.gpus = world
+    torch.cuda.set_device(local)
+    device = torch.device("cuda", local)
+    dist = init_dist(world, "nccl")
+    import cernels_b200  # noqa: F401  (loads the CUDA library; raises if missing)
+
+    cfg, case, kind, module = build_workload(args, device, rank, world)
+    step, inputs, launches = make_step(cfg, case, kind, module, world, rank)
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=device)
+    warmup = max(3, args.warmup)
+
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clocks:
+        total_ms, per = time_device(step, inputs, args.steps, warmup, flush, graph=args.graph)
+    torch.cuda.synchronize()
+    if world > 1:
+        t = torch.tensor([total_ms], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        total_ms = float(t.item())
+        dist.barrier()
+    e2e_ms, h2d, d2h = time_e2e(step, inputs, args.steps, warmup, flush)
+    if world > 1:
+        t = torch.tensor([e2e_ms], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        e2e_ms = float(t.item())
+
+    tokens = cfg.tokens
+    ms_per_step = total_ms / args.steps
+    value = tokens * args.steps / (total_ms / 1e3)
+    e2e_value = tokens * args.steps / (e2e_ms / 1e3)
+    roof = None
+    cpu = None
+    if rank == 0:
+        if world == 1 or cfg.name not in EP_CONFIGS:
+            roof = roofline(cfg, case, stage_profile(case, min(args.steps, 10)))
+        if world == 1 and not args.no_cpu_baseline:
+            cpu = cpu_oracle_baseline(case, args.cpu_sample_s)
+    if rank == 0:
+        line = {
+            "metric": "MoE-experts tokens/s", "value": round(value, 1), "unit": "tokens/s", "n_gpus": world,
+            "steps": args.steps, "warmup": warmup, "ms_per_step": round(ms_per_step, 4), "higher_is_better": True,
+            "scaling": "strong" if cfg.name in EP_CONFIGS else "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded; reference config shapes and distributions)",
+            "config": {"workload": cfg.name, "tokens": cfg.tokens, "hidden": cfg.hidden, "experts": cfg.experts,
+                       "intermediate": cfg.inter, "topk": cfg.topk, "shared_intermediate": cfg.shared_inter,
+                       "parallelism": f"ep{world}" if (world > 1 and cfg.name in EP_CONFIGS) else f"replica{world}",
+                       "l2": "flushed (256 MB write) before every timed step", "graph": bool(args.graph)},
+            "roofline": roof, "cpu_baseline": cpu,
+            "e2e": {"value": round(e2e_value, 1), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h},
+            "gpu_launches": launches * args.steps,
+            "clocks": clocks.summary(),
+            "op_roofline_ms": round(op_roofline_ms(cfg, case), 4),
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+def op_roofline_ms(cfg, case):
+    from cernels_b200.configs import touched_experts
+
+    hbm, tflops, _ = load_peaks()
+    e = touched_experts(case.indices, cfg.experts)
+    return max(cfg.flops() / (tflops * 1e12), cfg.bytes_moved(e) / (hbm * 1e9)) * 1e3
+
+
+def main(argv=None):
+    args = parse_args(argv)
+    if args.impl == "reference":
+        return run_reference(args)
+    return run_ours(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

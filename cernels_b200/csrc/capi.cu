@@ -164,29 +164,36 @@ static int validate_common(const cernels_moe_shape* shape, const void* x, const 
   return check_device();
 }
 
-int cernels_moe_experts(const cernels_moe_shape* shape, const void* x, const void* gate_up_proj,
-                        const float* gate_up_bias, const void* down_proj, const float* down_bias,
-                        const int32_t* indices, const float* weights, void* out, void* workspace,
-                        size_t workspace_bytes, void* stream_ptr) {
+// Launch sequence of the prefill path. When `events` is non-null, events[i] is recorded
+// before stage i and events[5] after the last stage.
+static int run_prefill(const cernels_moe_shape* shape, const void* x, const void* gate_up_proj,
+                       const float* gate_up_bias, const void* down_proj, const float* down_bias,
+                       const int32_t* indices, const float* weights, void* out, void* workspace,
+                       size_t workspace_bytes, cudaStream_t stream, cudaEvent_t* events) {
   const int rc0 = check_shape(shape);
   if (rc0) return rc0;
   const cernels_moe_shape s = *shape;
   int rc = validate_common(shape, x, gate_up_proj, down_proj, indices, weights, out, workspace, workspace_bytes,
                            prefill_workspace_bytes(s));
   if (rc || s.tokens == 0) return rc;
-  cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
   const PrefillWorkspace ws = carve_prefill_workspace(s, workspace);
   const int tk = s.tokens * s.topk;
   const bool gptoss = s.layout == CERNELS_LAYOUT_GPTOSS;
+  auto mark = [&](int i) {
+    if (events) cudaEventRecord(events[i], stream);
+  };
   cudaError_t err = cudaMemsetAsync(ws.status, 0, sizeof(int), stream);
   if (err != cudaSuccess) return cuda_rc(err);
 
+  mark(0);
   err = launch_route(indices, weights, s.tokens, s.topk, s.experts, ws, stream);
   if (err != cudaSuccess) return cuda_rc(err);
+  mark(1);
   // Rows at or past offsets[E] belong to no expert (skipped ids): not gathered, never read.
   err = launch_gather(static_cast<const __nv_bfloat16*>(x), ws.perm_token, tk, ws.offsets + s.experts, s.hidden,
                       ws.gathered, stream);
   if (err != cudaSuccess) return cuda_rc(err);
+  mark(2);
   const int sms = device_sm_count();
   GroupedGemmArgs g1{};
   g1.a = ws.gathered;
@@ -203,7 +210,7 @@ int cernels_moe_experts(const cernels_moe_shape* shape, const void* x, const voi
   g1.out_cols = s.intermediate;
   err = launch_grouped_gemm(gptoss ? kGateUpGptOss : kGateUpLinear, g1, sms, stream);
   if (err != cudaSuccess) return cuda_rc(err);
-
+  mark(3);
   GroupedGemmArgs g2{};
   g2.a = ws.glu;
   g2.b = static_cast<const __nv_bfloat16*>(down_proj);
@@ -219,10 +226,39 @@ int cernels_moe_experts(const cernels_moe_shape* shape, const void* x, const voi
   g2.out_cols = s.hidden;
   err = launch_grouped_gemm(gptoss ? kDownGptOss : kDownLinear, g2, sms, stream);
   if (err != cudaSuccess) return cuda_rc(err);
-
+  mark(4);
   err = launch_combine(ws.down_out, ws.inv, weights, s.tokens, s.topk, s.hidden, static_cast<__nv_bfloat16*>(out),
                        stream);
+  mark(5);
   return cuda_rc(err);
+}
+
+int cernels_moe_experts(const cernels_moe_shape* shape, const void* x, const void* gate_up_proj,
+                        const float* gate_up_bias, const void* down_proj, const float* down_bias,
+                        const int32_t* indices, const float* weights, void* out, void* workspace,
+                        size_t workspace_bytes, void* stream) {
+  return run_prefill(shape, x, gate_up_proj, gate_up_bias, down_proj, down_bias, indices, weights, out, workspace,
+                     workspace_bytes, static_cast<cudaStream_t>(stream), nullptr);
+}
+
+int cernels_moe_experts_profiled(const cernels_moe_shape* shape, const void* x, const void* gate_up_proj,
+                                 const float* gate_up_bias, const void* down_proj, const float* down_bias,
+                                 const int32_t* indices, const float* weights, void* out, void* workspace,
+                                 size_t workspace_bytes, void* stream_ptr, float* stage_ms) {
+  if (!stage_ms) return CERNELS_E_NULL;
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
+  cudaEvent_t ev[6];
+  for (int i = 0; i < 6; ++i)
+    if (cudaEventCreate(&ev[i]) != cudaSuccess) return CERNELS_E_CUDA;
+  int rc = run_prefill(shape, x, gate_up_proj, gate_up_bias, down_proj, down_bias, indices, weights, out, workspace,
+                       workspace_bytes, stream, ev);
+  if (rc == CERNELS_OK && shape->tokens > 0) {
+    cudaError_t err = cudaEventSynchronize(ev[5]);
+    for (int i = 0; i < 5 && err == cudaSuccess; ++i) err = cudaEventElapsedTime(&stage_ms[i], ev[i], ev[i + 1]);
+    rc = cuda_rc(err);
+  }
+  for (int i = 0; i < 6; ++i) cudaEventDestroy(ev[i]);
+  return rc;
 }
 
 int cernels_moe_experts_decode(const cernels_moe_shape* shape, const void* x, const void* gate_up_proj,

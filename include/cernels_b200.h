@@ -109,6 +109,15 @@ int cernels_moe_gather(const void* x, const int32_t* perm_token, int32_t rows, i
 int cernels_moe_combine(const void* rows, const int32_t* inv, const float* weights, int32_t tokens,
                         int32_t topk, int32_t hidden, void* out, void* stream);
 
+/* Diagnostics: runs cernels_moe_experts once with CUDA events recorded on `stream`
+ * between its stages and returns the device time of each stage in milliseconds:
+ * stage_ms[0] routing, [1] gather, [2] gate/up grouped GEMM, [3] down grouped GEMM,
+ * [4] combine. Synchronises `stream`. Not for the hot path. */
+int cernels_moe_experts_profiled(const cernels_moe_shape* shape, const void* x, const void* gate_up_proj,
+                                 const float* gate_up_bias, const void* down_proj, const float* down_bias,
+                                 const int32_t* indices, const float* weights, void* out, void* workspace,
+                                 size_t workspace_bytes, void* stream, float* stage_ms);
+
 /* Device status word of the last call that used this workspace (0 = ok; nonzero when a
  * bounded wait inside a kernel gave up). Reads device memory: synchronises `stream`. */
 int cernels_workspace_status(const cernels_moe_shape* shape, int decode, const void* workspace, int* status,
