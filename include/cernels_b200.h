@@ -118,6 +118,20 @@ int cernels_moe_experts_profiled(const cernels_moe_shape* shape, const void* x, 
                                  const int32_t* indices, const float* weights, void* out, void* workspace,
                                  size_t workspace_bytes, void* stream, float* stage_ms);
 
+/* Decode without any caller-provided scratch, for callers that cannot allocate device
+ * memory (no cudaMalloc available to them, or every device byte planned up front).
+ * No counterpart in the reference. Same math and kernels as cernels_moe_experts_decode;
+ * the scratch lives in a 4 MiB static __device__ array inside this library, held on each
+ * device that loads the library until the process exits. The first call on a device looks
+ * up that array's device address (cudaGetSymbolAddress), so make that first call before
+ * any stream capture. Problems needing more than 4 MiB of decode scratch (T*topk*(F+H)*4
+ * bytes plus a few KB), or T*topk > 1024, return CERNELS_E_UNSUPPORTED. All calls on a
+ * device share the one array: calls whose kernels may overlap on the GPU (different
+ * streams, or concurrent host threads) race and must be serialised by the caller. */
+int cernels_moe_experts_decode_noalloc(const cernels_moe_shape* shape, const void* x, const void* gate_up_proj,
+                                       const float* gate_up_bias, const void* down_proj, const float* down_bias,
+                                       const int32_t* indices, const float* weights, void* out, void* stream);
+
 /* Device status word of the last call that used this workspace (0 = ok; nonzero when a
  * bounded wait inside a kernel gave up). Reads device memory: synchronises `stream`. */
 int cernels_workspace_status(const cernels_moe_shape* shape, int decode, const void* workspace, int* status,
