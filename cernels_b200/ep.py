@@ -1,0 +1,164 @@
+"""Expert parallelism for the MoE-experts operators (one process per GPU).
+
+The reference is single-GPU; expert parallelism is the north star's multi-GPU scheme for
+the large-token configurations (qwen3_next, gpt_oss). Rank r of R owns the contiguous
+expert slice [r*E/R, (r+1)*E/R) and the contiguous token slice of its batch. One forward:
+
+  1. router on the local tokens (torch, as in the reference loaders)
+  2. routing kernel over the GLOBAL expert ids: offsets, stable permutation, inverse map
+     — rows bound for rank d are contiguous because experts are sharded contiguously
+  3. per-expert counts for each destination exchanged with all_to_all_single; one small
+     device->host copy gives the split sizes NCCL needs
+  4. gather kernel builds the send buffer (local token rows in routed order)
+  5. dispatch all_to_all_single (NCCL over NVLink) -> rows for my experts, ordered by
+     (source rank, local expert)
+  6. local experts: the experts operator with topk = 1 over the received rows
+     (local expert id per row, weight 1), i.e. the grouped tcgen05 GEMMs + bias
+  7. combine all_to_all_single back -> every row returns to its source position
+  8. combine kernel: out[t] = sum_j w[t, j] * row[inv[t, j]] in fp32, slot order
+  (qwen3_next adds its gated shared expert on the local tokens.)
+
+All device work goes through a ``Backend`` (the CUDA kernels by default). Tests run the
+same exchange logic on CPU gloo ranks with a CPU backend.
+"""
+
+from __future__ import annotations
+
+import dataclasses
+from typing import Callable
+
+import torch
+import torch.distributed as dist
+
+
+def token_shard(tokens: int, rank: int, world: int) -> slice:
+    """Contiguous token slice of rank `rank` (first `tokens % world` ranks get one more)."""
+    base, rem = divmod(tokens, world)
+    start = rank * base + min(rank, rem)
+    return slice(start, start + base + (1 if rank < rem else 0))
+
+
+def expert_shard(experts: int, rank: int, world: int) -> tuple[int, int]:
+    if experts % world:
+        raise ValueError(f"{experts} experts do not split evenly over {world} ranks")
+    per = experts // world
+    return rank * per, (rank + 1) * per
+
+
+@dataclasses.dataclass
+class Backend:
+    """Device operations the EP forward needs.
+
+    route(indices int32 [T,k], weights fp32 [T,k], E) -> (offsets [E+1], perm_token, perm_weight, inv)
+    gather(x [T,H], perm_token, rows) -> [rows, H]
+    experts(rows [N,H], local_idx int32 [N,1], ones fp32 [N,1]) -> [N,H] (unweighted, + bias)
+    combine(rows [M,H], inv int32 [T*k], weights fp32 [T,k]) -> [T,H]
+    """
+
+    route: Callable
+    gather: Callable
+    experts: Callable
+    combine: Callable
+
+
+def cuda_backend(layout: int, w1: torch.Tensor, w2: torch.Tensor, b1=None, b2=None) -> Backend:
+    from . import ops
+
+    def experts(rows, local_idx, ones):
+        return ops.run_experts(rows, w1, w2, local_idx, ones, 1, layout, False, b1, b2)
+
+    return Backend(route=ops.route, gather=ops.gather_rows, experts=experts, combine=ops.combine_rows)
+
+
+class ExpertParallelMoe:
+    """EP forward over a process group; weights of the local expert slice only."""
+
+    def __init__(self, experts: int, topk: int, rank: int, world: int, router: Callable, backend: Backend,
+                 shared: Callable | None = None, group=None):
+        self.E = experts
+        self.k = topk
+        self.rank = rank
+        self.world = world
+        self.e0, self.e1 = expert_shard(experts, rank, world)
+        self.router = router
+        self.backend = backend
+        self.shared = shared
+        self.group = group
+        # route(3) + gather(1) + local experts op(7) + combine(1); + 7 for the shared expert
+        self.launches_per_step = 12 + (7 if shared is not None else 0)
+
+    # ------------------------------------------------------------ construction
+    @classmethod
+    def from_module(cls, kind: str, module, rank: int, world: int, group=None) -> "ExpertParallelMoe":
+        from .configs import LAYOUT_GPTOSS, LAYOUT_LINEAR
+
+        if kind == "gpt_oss":
+            ex = module.experts
+            E = ex.gate_up_proj.shape[0]
+            e0, e1 = expert_shard(E, rank, world)
+            w1 = ex.gate_up_proj.data[e0:e1].contiguous()
+            w2 = ex.down_proj.data[e0:e1].contiguous()
+            b1 = ex.gate_up_proj_bias.data[e0:e1].float().contiguous()
+            b2 = ex.down_proj_bias.data[e0:e1].float().contiguous()
+            backend = cuda_backend(LAYOUT_GPTOSS, w1, w2, b1, b2)
+
+            def router(x):
+                _, scores, idx = module.router(x)
+                return idx, scores
+
+            return cls(E, int(module.router.top_k), rank, world, router, backend, None, group)
+        if kind == "qwen3_next":
+            from .registry import qwen3_next_moe_experts as qn
+
+            ex = module.experts
+            E = ex.gate_up_proj.shape[0]
+            e0, e1 = expert_shard(E, rank, world)
+            backend = cuda_backend(LAYOUT_LINEAR, ex.gate_up_proj.data[e0:e1].contiguous(),
+                                   ex.down_proj.data[e0:e1].contiguous())
+
+            def router(x):
+                _, scores, idx = module.gate(x)
+                return idx, scores
+
+            return cls(E, int(module.gate.top_k), rank, world, router, backend, lambda x: qn.shared_expert(x, module),
+                       group)
+        raise ValueError(f"expert parallelism is not used for {kind}")
+
+    # ------------------------------------------------------------ forward
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        R, E, k = self.world, self.E, self.k
+        per = E // R
+        dev = x.device
+        with torch.no_grad():
+            idx, w = self.router(x)
+            idx = idx.to(torch.int32).contiguous()
+            w = w.float().contiguous()
+            T = x.shape[0]
+            offsets, perm_token, _perm_weight, inv = self.backend.route(idx, w, E)
+            # per-expert counts, grouped by destination rank -> [R, per]
+            send_counts = (offsets[1:] - offsets[:-1]).to(torch.int64).reshape(R, per)
+            recv_counts = torch.empty_like(send_counts)
+            dist.all_to_all_single(recv_counts, send_counts, group=self.group)
+            counts_host = torch.stack([send_counts.sum(1), recv_counts.sum(1)]).cpu()  # one small D2H
+            send_splits = counts_host[0].tolist()
+            recv_splits = counts_host[1].tolist()
+            n_send = int(sum(send_splits))
+            n_recv = int(sum(recv_splits))
+            H = x.shape[1]
+            send_buf = self.backend.gather(x, perm_token, n_send) if n_send else x.new_empty(0, H)
+            recv_buf = x.new_empty(n_recv, H)
+            dist.all_to_all_single(recv_buf, send_buf, recv_splits, send_splits, group=self.group)
+            if n_recv:
+                local_idx = torch.repeat_interleave(
+                    torch.arange(per, device=dev, dtype=torch.int32).repeat(R), recv_counts.reshape(-1),
+                    output_size=n_recv).reshape(n_recv, 1).contiguous()
+                ones = torch.ones(n_recv, 1, dtype=torch.float32, device=dev)
+                rows_out = self.backend.experts(recv_buf, local_idx, ones)
+            else:
+                rows_out = x.new_empty(0, H)
+            back = x.new_empty(n_send, H)
+            dist.all_to_all_single(back, rows_out, send_splits, recv_splits, group=self.group)
+            out = self.backend.combine(back, inv, w)
+            if self.shared is not None:
+                out = out + self.shared(x)
+            return out

@@ -1,0 +1,75 @@
+"""GPU: expert parallelism over NCCL on every visible GPU (skipped with fewer than 2).
+
+Each rank runs the EP forward on its token shard; its rows must match the single-GPU
+operator on the full batch (same kernels, so only bf16 rounding order of the combine may
+differ — the parity tolerance applies).
+"""
+
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.multiprocessing as mp
+
+pytestmark = pytest.mark.gpu
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def _worker(rank, world, port, cfg_name, tokens, q):
+    import datetime
+
+    import torch.distributed as dist
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=120),
+                            device_id=torch.device("cuda", rank))
+    try:
+        from cernels_b200 import ep
+        from cernels_b200.configs import CONFIGS, make_case
+        from cernels_b200.hf_modules import build_module
+        from cernels_b200.registry import gpt_oss_moe_experts as go
+        from cernels_b200.registry import qwen3_next_moe_experts as qn
+        from oracle import moe_oracle as O
+
+        cfg = CONFIGS[cfg_name].with_tokens(tokens)
+        case = make_case(cfg, device=f"cuda:{rank}")
+        kind, module = build_module(case)
+        moe = ep.ExpertParallelMoe.from_module(kind, module, rank, world)
+        shard = ep.token_shard(cfg.tokens, rank, world)
+        out = moe.forward(case.x[shard].contiguous())
+        full = (go.kernel if kind == "gpt_oss" else qn.kernel)(case.x.unsqueeze(0), module).squeeze(0)
+        torch.cuda.synchronize()
+        err = O.rel_err(out.float().cpu().numpy(), full[shard].float().cpu().numpy())
+        q.put((rank, err))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("cfg_name,tokens", [("gpt_oss_20b", 2048), ("qwen3_next", 1024)])
+def test_ep_matches_single_gpu(cfg_name, tokens):
+    world = torch.cuda.device_count()
+    if world < 2:
+        pytest.skip("needs 2 or more GPUs")
+    world = 2 if world < 4 else (4 if world < 8 else 8)
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, world, port, cfg_name, tokens, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    errs = dict(q.get(timeout=600) for _ in range(world))
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    assert max(errs.values()) <= 1e-2, errs
