@@ -18,7 +18,10 @@
 // 16-byte loads along K and a warp-shuffle reduction. GPTOSS weights ([E,H,2F], [E,F,H])
 // are N-contiguous: each lane owns 8 adjacent output columns, warps split K and reduce
 // through shared memory.
+#include <algorithm>
+
 #include "moe_internal.h"
+#include "sm100_primitives.cuh"
 
 namespace cernels {
 namespace {
@@ -31,6 +34,13 @@ constexpr int kRowsPerCta = kDecWarps * kRowsPerWarp;  // 16
 constexpr int kColsPerCta = 256;      // GPTOSS: output columns per CTA (32 lanes x 8)
 constexpr float kLimit = 7.0f;
 constexpr float kAlpha = 1.702f;
+constexpr unsigned long long kBarrierLimitNs = 2000000000ull;
+
+__device__ __forceinline__ unsigned long long global_timer_ns_dec() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+  return t;
+}
 
 struct Grouping {
   int expert;     // expert id of this CTA's group (-1: no such group)
@@ -465,6 +475,274 @@ __global__ void __launch_bounds__(kDecThreads) decode_down_gptoss(
                scratch + 3);
 }
 
+// ---------------------------------------------------------------- fused persistent LINEAR decode
+// One cooperative launch: every CTA builds the expert grouping once, then loops over
+// (group, 16-row block) units of the gate/up stage, crosses a bounded grid barrier, and
+// loops over (group, 16-row block) units of the down stage; the last unit to finish an
+// output block combines it (fixed slot order). Requires T * H * 2 and 8 * F * 4 bytes of
+// shared memory (x rows of all tokens, then one batch of fp32 activation rows).
+constexpr int kFusedMaxPairs = 256;
+
+struct FusedGroups {
+  int n_groups;
+  int expert[kFusedMaxPairs];
+  int start[kFusedMaxPairs + 1];
+  int count[kFusedMaxPairs];
+  int list[kFusedMaxPairs];
+  int word_prefix[kBitmapWords];
+  unsigned bitmap[kBitmapWords];
+  int flag;
+};
+
+__device__ void build_groups_fused(const int32_t* __restrict__ indices, int total, int experts, FusedGroups& G) {
+  const int words = (experts + 31) >> 5;
+  for (int w = threadIdx.x; w < words; w += blockDim.x) G.bitmap[w] = 0u;
+  for (int i = threadIdx.x; i < total; i += blockDim.x) G.count[i] = 0;
+  __syncthreads();
+  for (int i = threadIdx.x; i < total; i += blockDim.x) {
+    const int e = indices[i];
+    if (e >= 0 && e < experts) atomicOr(&G.bitmap[e >> 5], 1u << (e & 31));
+  }
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    const int lane = threadIdx.x;
+    int carry = 0;
+    for (int w0 = 0; w0 < words; w0 += 32) {
+      const int w = w0 + lane;
+      const int c = w < words ? __popc(G.bitmap[w]) : 0;
+      int incl = c;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int n = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += n;
+      }
+      if (w < words) G.word_prefix[w] = carry + incl - c;
+      carry += __shfl_sync(0xffffffffu, incl, 31);
+    }
+    if (lane == 0) G.n_groups = carry;
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < total; i += blockDim.x) {
+    const int e = indices[i];
+    if (e < 0 || e >= experts) continue;
+    const int g = G.word_prefix[e >> 5] + __popc(G.bitmap[e >> 5] & ((1u << (e & 31)) - 1u));
+    G.expert[g] = e;
+    atomicAdd(&G.count[g], 1);
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    int acc = 0;
+    for (int g = 0; g < G.n_groups; ++g) {
+      G.start[g] = acc;
+      acc += G.count[g];
+      G.count[g] = 0;  // reused as fill cursor
+    }
+    G.start[G.n_groups] = acc;
+  }
+  __syncthreads();
+  // Order inside a group does not affect results: each pair's row is computed by the same
+  // lanes in the same order whatever its batch slot.
+  for (int i = threadIdx.x; i < total; i += blockDim.x) {
+    const int e = indices[i];
+    if (e < 0 || e >= experts) continue;
+    const int g = G.word_prefix[e >> 5] + __popc(G.bitmap[e >> 5] & ((1u << (e & 31)) - 1u));
+    G.list[G.start[g] + atomicAdd(&G.count[g], 1)] = i;
+  }
+  __syncthreads();
+}
+
+// Grid-wide barrier for a cooperative launch. bar[0] = arrivals, bar[1] = generation.
+// Bounded: gives up after kWaitLimitNs, records `code` in *status and returns false.
+__device__ bool grid_barrier_bounded(unsigned* bar, unsigned n_blocks, int* status, int code, int* flag) {
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    *flag = 1;
+    volatile unsigned* vgen = bar + 1;
+    const unsigned gen = *vgen;
+    __threadfence();
+    const unsigned arrived = atomicAdd(bar, 1u);
+    if (arrived == n_blocks - 1) {
+      atomicExch(bar, 0u);
+      __threadfence();
+      atomicAdd(bar + 1, 1u);
+    } else {
+      const unsigned long long t0 = global_timer_ns_dec();
+      while (*vgen == gen) {
+        __nanosleep(64);
+        if (global_timer_ns_dec() - t0 > kBarrierLimitNs) {
+          if (status) atomicCAS(status, 0, code);
+          *flag = 0;
+          break;
+        }
+      }
+    }
+    __threadfence();
+  }
+  __syncthreads();
+  return *flag != 0;
+}
+
+__global__ void __launch_bounds__(kDecThreads) decode_fused_linear(
+    const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ w1, const __nv_bfloat16* __restrict__ w2,
+    const int32_t* __restrict__ indices, const float* __restrict__ weights, int tokens, int topk, int experts, int H,
+    int F, float* __restrict__ glu, float* __restrict__ partial, int* __restrict__ counters,
+    unsigned* __restrict__ barrier, int* __restrict__ status, __nv_bfloat16* __restrict__ out) {
+  extern __shared__ __align__(16) uint8_t dsm_raw[];
+  FusedGroups& G = *reinterpret_cast<FusedGroups*>(dsm_raw);
+  uint8_t* buf = dsm_raw + ((sizeof(FusedGroups) + 15) & ~size_t(15));
+  const int total = tokens * topk;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int hv = H / 8, fv = F / 8;
+
+  // x rows of every token, bf16, in shared memory (phase 1 operand)
+  uint4* xs = reinterpret_cast<uint4*>(buf);
+  for (int i = threadIdx.x; i < tokens * hv; i += blockDim.x)
+    xs[i] = reinterpret_cast<const uint4*>(x)[i];
+  build_groups_fused(indices, total, experts, G);
+  const int n_groups = G.n_groups;
+
+  // ---- phase 1: gate/up + activation -> glu[pair, f] (fp32)
+  const int nfb = (F + kRowsPerCta - 1) / kRowsPerCta;
+  for (int u = blockIdx.x; u < n_groups * nfb; u += gridDim.x) {
+    const int g = u / nfb, fb = u - (u / nfb) * nfb;
+    const uint4* wg = reinterpret_cast<const uint4*>(w1 + static_cast<size_t>(G.expert[g]) * 2 * F * H);
+    const int f0 = fb * kRowsPerCta + warp * kRowsPerWarp;
+    size_t row_off[2 * kRowsPerWarp];
+#pragma unroll
+    for (int r = 0; r < kRowsPerWarp; ++r) {
+      const int f = min(f0 + r, F - 1);
+      row_off[r] = static_cast<size_t>(f) * hv;
+      row_off[kRowsPerWarp + r] = static_cast<size_t>(F + f) * hv;
+    }
+    const int p_begin = G.start[g], p_end = G.start[g + 1];
+    for (int p0 = p_begin; p0 < p_end; p0 += kTokBatch) {
+      const int nb = min(kTokBatch, p_end - p0);
+      int tok[kTokBatch];
+#pragma unroll
+      for (int b = 0; b < kTokBatch; ++b) tok[b] = b < nb ? G.list[p0 + b] / topk : 0;
+      float acc[2 * kRowsPerWarp][kTokBatch];
+#pragma unroll
+      for (int r = 0; r < 2 * kRowsPerWarp; ++r)
+#pragma unroll
+        for (int b = 0; b < kTokBatch; ++b) acc[r][b] = 0.f;
+#pragma unroll 2
+      for (int v = lane; v < hv; v += 32) {
+        uint4 wv[2 * kRowsPerWarp];
+#pragma unroll
+        for (int r = 0; r < 2 * kRowsPerWarp; ++r) wv[r] = __ldg(wg + row_off[r] + v);
+        float wf[2 * kRowsPerWarp][8];
+#pragma unroll
+        for (int r = 0; r < 2 * kRowsPerWarp; ++r) bf16x8_to_f32(wv[r], wf[r]);
+#pragma unroll
+        for (int b = 0; b < kTokBatch; ++b) {
+          if (b < nb) {
+            float xf[8];
+            bf16x8_to_f32(xs[tok[b] * hv + v], xf);
+#pragma unroll
+            for (int r = 0; r < 2 * kRowsPerWarp; ++r)
+#pragma unroll
+              for (int i = 0; i < 8; ++i) acc[r][b] = fmaf(wf[r][i], xf[i], acc[r][b]);
+          }
+        }
+      }
+#pragma unroll
+      for (int b = 0; b < kTokBatch; ++b) {
+        if (b < nb) {
+#pragma unroll
+          for (int r = 0; r < kRowsPerWarp; ++r) {
+            const float gsum = warp_sum(acc[r][b]);
+            const float usum = warp_sum(acc[kRowsPerWarp + r][b]);
+            const int f = f0 + r;
+            if (lane == 0 && f < F) glu[static_cast<size_t>(G.list[p0 + b]) * F + f] = act_linear(gsum, usum);
+          }
+        }
+      }
+    }
+  }
+
+  if (!grid_barrier_bounded(barrier, gridDim.x, status, kStatusTimeoutOther, &G.flag)) return;
+
+  // ---- phase 2: down -> partial[pair, h]; last unit of an h-block combines it
+  const int nhb = (H + kRowsPerCta - 1) / kRowsPerCta;
+  float4* gs = reinterpret_cast<float4*>(buf);  // [kTokBatch, F/4] (reuses the x area)
+  if (n_groups == 0) {
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < tokens * H; i += gridDim.x * blockDim.x)
+      out[i] = __float2bfloat16_rn(0.f);
+    return;
+  }
+  for (int u = blockIdx.x; u < n_groups * nhb; u += gridDim.x) {
+    const int g = u / nhb, hb = u - (u / nhb) * nhb;
+    const uint4* wd = reinterpret_cast<const uint4*>(w2 + static_cast<size_t>(G.expert[g]) * H * F);
+    const int h0 = hb * kRowsPerCta + warp * kRowsPerWarp;
+    size_t row_off[kRowsPerWarp];
+#pragma unroll
+    for (int r = 0; r < kRowsPerWarp; ++r) row_off[r] = static_cast<size_t>(min(h0 + r, H - 1)) * fv;
+    const int p_begin = G.start[g], p_end = G.start[g + 1];
+    for (int p0 = p_begin; p0 < p_end; p0 += kTokBatch) {
+      const int nb = min(kTokBatch, p_end - p0);
+      __syncthreads();
+      for (int i = threadIdx.x; i < nb * (F / 4); i += blockDim.x) {
+        const int r = i / (F / 4), v = i - r * (F / 4);
+        gs[r * (F / 4) + v] = __ldcg(reinterpret_cast<const float4*>(glu + static_cast<size_t>(G.list[p0 + r]) * F) + v);
+      }
+      __syncthreads();
+      float acc[kRowsPerWarp][kTokBatch];
+#pragma unroll
+      for (int r = 0; r < kRowsPerWarp; ++r)
+#pragma unroll
+        for (int b = 0; b < kTokBatch; ++b) acc[r][b] = 0.f;
+#pragma unroll 4
+      for (int v = lane; v < fv; v += 32) {
+        float wf[kRowsPerWarp][8];
+#pragma unroll
+        for (int r = 0; r < kRowsPerWarp; ++r) bf16x8_to_f32(__ldg(wd + row_off[r] + v), wf[r]);
+#pragma unroll
+        for (int b = 0; b < kTokBatch; ++b) {
+          if (b < nb) {
+            const float4 ga = gs[b * (F / 4) + 2 * v];
+            const float4 gb = gs[b * (F / 4) + 2 * v + 1];
+            const float gf[8] = {ga.x, ga.y, ga.z, ga.w, gb.x, gb.y, gb.z, gb.w};
+#pragma unroll
+            for (int r = 0; r < kRowsPerWarp; ++r)
+#pragma unroll
+              for (int i = 0; i < 8; ++i) acc[r][b] = fmaf(wf[r][i], gf[i], acc[r][b]);
+          }
+        }
+      }
+#pragma unroll
+      for (int b = 0; b < kTokBatch; ++b) {
+        if (b < nb) {
+#pragma unroll
+          for (int r = 0; r < kRowsPerWarp; ++r) {
+            const float sum = warp_sum(acc[r][b]);
+            if (lane == 0 && h0 + r < H) partial[static_cast<size_t>(G.list[p0 + b]) * H + h0 + r] = sum;
+          }
+        }
+      }
+    }
+    // arrival on this h-block; the last of the n_groups units combines it
+    __threadfence();
+    __syncthreads();
+    if (threadIdx.x == 0) G.flag = atomicAdd(&counters[hb], 1) == n_groups - 1;
+    __syncthreads();
+    if (G.flag) {
+      __threadfence();
+      const int c0 = hb * kRowsPerCta, c1 = min(H, c0 + kRowsPerCta), width = c1 - c0;
+      for (int i = threadIdx.x; i < tokens * width; i += blockDim.x) {
+        const int t = i / width, c = c0 + (i - t * width);
+        float s = 0.f;
+        for (int j = 0; j < topk; ++j) {
+          const int p = t * topk + j;
+          const int e = indices[p];
+          if (e < 0 || e >= experts) continue;
+          s = fmaf(weights[p], __ldcg(partial + static_cast<size_t>(p) * H + c), s);
+        }
+        out[static_cast<size_t>(t) * H + c] = __float2bfloat16_rn(s);
+      }
+    }
+  }
+}
+
 }  // namespace
 
 cudaError_t launch_decode(const DecodeArgs& a, const DecodeWorkspace& ws, cudaStream_t stream) {
@@ -473,6 +751,45 @@ cudaError_t launch_decode(const DecodeArgs& a, const DecodeWorkspace& ws, cudaSt
   const int max_groups = total < a.experts ? total : a.experts;
   const int H = a.hidden, F = a.inter;
   cudaError_t err;
+  if (a.layout == CERNELS_LAYOUT_LINEAR && total <= kFusedMaxPairs) {
+    const size_t operand = std::max(static_cast<size_t>(a.tokens) * H * 2, static_cast<size_t>(kTokBatch) * F * 4);
+    const size_t smem = ((sizeof(FusedGroups) + 15) & ~size_t(15)) + operand;
+    if (smem <= 200 * 1024) {
+      static int attr_smem = 0;
+      if (static_cast<int>(smem) > attr_smem) {
+        if ((err = cudaFuncSetAttribute(decode_fused_linear, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        200 * 1024)) != cudaSuccess)
+          return err;
+        attr_smem = 200 * 1024;
+      }
+      int per_sm = 0;
+      if ((err = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, decode_fused_linear, kDecThreads, smem)) !=
+          cudaSuccess)
+        return err;
+      const int n_hblocks = (H + kRowsPerCta - 1) / kRowsPerCta;
+      const int n_fblocks = (F + kRowsPerCta - 1) / kRowsPerCta;
+      const int units = max_groups * std::max(n_hblocks, n_fblocks);
+      int grid = std::min(per_sm * device_sm_count(), units);
+      if (grid < 1) grid = 1;
+      // arrival counters [n_hblocks] and the grid barrier [2] start at zero
+      if ((err = cudaMemsetAsync(ws.counters, 0, (n_hblocks + 2) * sizeof(int), stream)) != cudaSuccess) return err;
+      cudaLaunchConfig_t cfg = {};
+      cfg.gridDim = dim3(grid);
+      cfg.blockDim = dim3(kDecThreads);
+      cfg.dynamicSmemBytes = smem;
+      cfg.stream = stream;
+      cudaLaunchAttribute attr[1];
+      attr[0].id = cudaLaunchAttributeCooperative;
+      attr[0].val.cooperative = 1;
+      cfg.attrs = attr;
+      cfg.numAttrs = 1;
+      err = cudaLaunchKernelEx(&cfg, decode_fused_linear, a.x, a.w1, a.w2, a.indices, a.weights, a.tokens, a.topk,
+                               a.experts, H, F, ws.glu, ws.partial, ws.counters,
+                               reinterpret_cast<unsigned*>(ws.counters + n_hblocks), ws.status, a.out);
+      if (err != cudaSuccess) return err;
+      return cudaGetLastError();
+    }
+  }
   if (a.layout == CERNELS_LAYOUT_LINEAR) {
     const size_t smem1 = kHeaderBytes + static_cast<size_t>(kTokBatch) * H * 2;
     const size_t smem2 = kHeaderBytes + static_cast<size_t>(kTokBatch) * F * 4;

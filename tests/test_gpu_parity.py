@@ -155,7 +155,7 @@ def test_empty_batch():
 
 # ---------------------------------------------------------------- decode
 @pytest.mark.parametrize("layout", [LAYOUT_LINEAR, LAYOUT_GPTOSS])
-@pytest.mark.parametrize("T", [1, 2, 4, 8, 33])
+@pytest.mark.parametrize("T", [1, 2, 4, 8, 33, 60])
 def test_decode_matches_oracle_and_prefill(T, layout):
     g = torch.Generator().manual_seed(100 + T)
     H, E, F, k = (2048, 64, 1408, 6) if layout == LAYOUT_LINEAR else (2880, 32, 2880, 4)
@@ -221,3 +221,33 @@ def test_decode_config(T):
     out = run_op(case.x, case.w1, case.w2, case.indices, case.weights, 6, LAYOUT_LINEAR, True)
     ref = oracle_out(case.x, case.w1, case.w2, case.indices, case.weights, LAYOUT_LINEAR)
     assert_close(out, ref)
+
+
+@pytest.mark.parametrize("decode", [False, True])
+def test_cuda_graph_capture_and_replay(decode):
+    """No host sync inside the op: it captures into a CUDA graph, and replays see new inputs."""
+    g = torch.Generator().manual_seed(21)
+    T, H, E, F, k = 8, 2048, 64, 1408, 6
+    w1 = (torch.randn(E, 2 * F, H, generator=g) * 0.02).to(torch.bfloat16).to(DEV)
+    w2 = (torch.randn(E, H, F, generator=g) * 0.02).to(torch.bfloat16).to(DEV)
+    x = torch.randn(T, H, generator=g).to(torch.bfloat16).to(DEV)
+    idx = torch.randint(0, E, (T, k), generator=g).to(torch.int32).to(DEV)
+    w = torch.rand(T, k, generator=g).to(DEV)
+    fn = ops.cohere2_moe_experts_decode if decode else ops.cohere2_moe_experts
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        fn(x, w1, w2, idx, w, k)  # warm-up (sets kernel attributes outside capture)
+    torch.cuda.current_stream().wait_stream(s)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        out = fn(x, w1, w2, idx, w, k)
+    for seed in (1, 2):
+        gg = torch.Generator().manual_seed(seed)
+        x.copy_(torch.randn(T, H, generator=gg).to(torch.bfloat16))
+        idx.copy_(torch.randint(0, E, (T, k), generator=gg).to(torch.int32))
+        graph.replay()
+        torch.cuda.synchronize()
+        eager = fn(x, w1, w2, idx, w, k)
+        assert torch.equal(out, eager)
