@@ -267,6 +267,40 @@ def stage_profile(case, steps):
     return [a / n for a in acc]
 
 
+def decode_roofline(case, steps):
+    """Decode op (its kernels only: int32/fp32 routing inputs prepared outside) timed with CUDA
+    events, L2 flushed before each call; bound = HBM on the touched experts' weights."""
+    import torch
+
+    from cernels_b200 import ops
+    from cernels_b200.configs import touched_experts
+
+    cfg = case.cfg
+    idx = case.indices.to(torch.int32).contiguous()
+    w = case.weights.float().contiguous()
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=case.x.device)
+    stream = torch.cuda.current_stream()
+    total = 0.0
+    for i in range(steps + 3):
+        flush.zero_()
+        a = torch.cuda.Event(enable_timing=True)
+        b = torch.cuda.Event(enable_timing=True)
+        a.record(stream)
+        ops.run_experts(case.x, case.w1, case.w2, idx, w, cfg.topk, cfg.layout, True, case.b1, case.b2)
+        b.record(stream)
+        b.synchronize()
+        if i >= 3:
+            total += a.elapsed_time(b)
+    ms = total / steps
+    hbm, _, src = load_peaks()
+    e = touched_experts(case.indices, cfg.experts)
+    bytes_ = 3.0 * cfg.hidden * cfg.inter * 2 * e + 2.0 * cfg.tokens * cfg.hidden * 2
+    achieved = bytes_ / (ms / 1e3) / 1e9
+    return {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
+            "frac": round(achieved / hbm, 4), "kernel": "decode op (decode_fused_linear)", "peak_source": src,
+            "traffic": None, "op_ms": round(ms, 4), "algorithmic": {"bytes": bytes_, "touched_experts": e}}
+
+
 def load_peaks():
     path = os.path.join(ROOT, "MEASURED_PEAKS.json")
     try:
@@ -441,7 +475,9 @@ def run_ours(args):
     roof = None
     cpu = None
     if rank == 0:
-        if world == 1 or cfg.name not in EP_CONFIGS:
+        if cfg.name == "decode":
+            roof = decode_roofline(case, min(args.steps, 20))
+        elif world == 1 or cfg.name not in EP_CONFIGS:
             roof = roofline(cfg, case, stage_profile(case, min(args.steps, 10)))
         if world == 1 and not args.no_cpu_baseline:
             cpu = cpu_oracle_baseline(case, args.cpu_sample_s)
