@@ -582,164 +582,269 @@ __device__ bool grid_barrier_bounded(unsigned* bar, unsigned n_blocks, int* stat
   return *flag != 0;
 }
 
-__global__ void __launch_bounds__(kDecThreads) decode_fused_linear(
+// ---------------------------------------------------------------- streaming LINEAR decode
+// One cooperative launch, one CTA per SM, 9 warps. Warp 8 (one lane) streams weight rows
+// with cp.async.bulk into a ring of kStreamStages x kStreamStageBytes of shared memory
+// (completion counted on mbarriers), so ~144 KB per SM are in flight without occupying
+// registers; warps 0-7 compute from shared memory. Each CTA builds the expert grouping
+// once, then:
+//   phase 1  units (group, token batch of <= 8, R1 gate/up row pairs): glu[pair, f] fp32
+//   barrier  (bounded, grid-wide)
+//   phase 2  units (group, token batch of <= B2, R2 down rows); the stage also carries
+//            the batch's fp32 glu rows: partial[pair, h] fp32
+//   barrier
+//   phase 3  out[t, h] = bf16(sum_j w[t, j] * partial[(t, j), h]) in slot order
+constexpr int kStreamStages = 3;
+constexpr int kStreamStageBytes = 48 * 1024;
+constexpr int kStreamConsumers = 8;
+constexpr int kStreamThreads = (kStreamConsumers + 1) * 32;
+
+struct StreamPlan {
+  int r1, nfr;       // phase 1: f rows per stage, stages per (group, batch)
+  int b2, r2, nhr;   // phase 2: tokens per batch, h rows per stage, stages per (group, batch)
+};
+
+__host__ __device__ inline StreamPlan make_stream_plan(int H, int F) {
+  StreamPlan p;
+  p.r1 = kStreamStageBytes / (4 * H);
+  if (p.r1 > kStreamConsumers) p.r1 = kStreamConsumers;
+  p.nfr = p.r1 > 0 ? (F + p.r1 - 1) / p.r1 : 0;
+  // Tokens per phase-2 batch: as many as fit next to 8 down rows, at least one.
+  p.b2 = (kStreamStageBytes - 8 * 2 * F) / (4 * F);
+  if (p.b2 < 1) p.b2 = (kStreamStageBytes - 2 * F) / (4 * F) > 0 ? 1 : 0;
+  if (p.b2 > kTokBatch) p.b2 = kTokBatch;
+  p.r2 = p.b2 > 0 ? (kStreamStageBytes - p.b2 * 4 * F) / (2 * F) : 0;
+  if (p.r2 > 4 * kStreamConsumers) p.r2 = 4 * kStreamConsumers;
+  p.nhr = p.r2 > 0 ? (H + p.r2 - 1) / p.r2 : 0;
+  return p;
+}
+
+struct StreamShared {
+  FusedGroups G;
+  int batch1_prefix[kFusedMaxPairs + 1];  // phase-1 token batches before group g
+  int batch2_prefix[kFusedMaxPairs + 1];
+  uint64_t full[kStreamStages];
+  uint64_t empty[kStreamStages];
+  int abort;
+};
+
+__device__ __forceinline__ int find_group(const int* prefix, int n_groups, int q) {
+  int lo = 0, hi = n_groups - 1;
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (prefix[mid] <= q) lo = mid; else hi = mid - 1;
+  }
+  return lo;
+}
+
+__global__ void __launch_bounds__(kStreamThreads, 1) decode_stream_linear(
     const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ w1, const __nv_bfloat16* __restrict__ w2,
     const int32_t* __restrict__ indices, const float* __restrict__ weights, int tokens, int topk, int experts, int H,
-    int F, float* __restrict__ glu, float* __restrict__ partial, int* __restrict__ counters,
-    unsigned* __restrict__ barrier, int* __restrict__ status, __nv_bfloat16* __restrict__ out) {
-  extern __shared__ __align__(16) uint8_t dsm_raw[];
-  FusedGroups& G = *reinterpret_cast<FusedGroups*>(dsm_raw);
-  uint8_t* buf = dsm_raw + ((sizeof(FusedGroups) + 15) & ~size_t(15));
+    int F, float* __restrict__ glu, float* __restrict__ partial, unsigned* __restrict__ barrier,
+    int* __restrict__ status, __nv_bfloat16* __restrict__ out) {
+  extern __shared__ __align__(128) uint8_t dsm_raw[];
+  StreamShared& S = *reinterpret_cast<StreamShared*>(dsm_raw);
+  uint8_t* ring = dsm_raw + ((sizeof(StreamShared) + 127) & ~size_t(127));
+  uint4* xs = reinterpret_cast<uint4*>(ring + kStreamStages * kStreamStageBytes);  // [tokens, H/8]
+  FusedGroups& G = S.G;
   const int total = tokens * topk;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int hv = H / 8, fv = F / 8;
+  const StreamPlan plan = make_stream_plan(H, F);
+  volatile int* abort_flag = &S.abort;
 
-  // x rows of every token, bf16, in shared memory (phase 1 operand)
-  uint4* xs = reinterpret_cast<uint4*>(buf);
-  for (int i = threadIdx.x; i < tokens * hv; i += blockDim.x)
-    xs[i] = reinterpret_cast<const uint4*>(x)[i];
-  build_groups_fused(indices, total, experts, G);
-  const int n_groups = G.n_groups;
-
-  // ---- phase 1: gate/up + activation -> glu[pair, f] (fp32)
-  const int nfb = (F + kRowsPerCta - 1) / kRowsPerCta;
-  for (int u = blockIdx.x; u < n_groups * nfb; u += gridDim.x) {
-    const int g = u / nfb, fb = u - (u / nfb) * nfb;
-    const uint4* wg = reinterpret_cast<const uint4*>(w1 + static_cast<size_t>(G.expert[g]) * 2 * F * H);
-    const int f0 = fb * kRowsPerCta + warp * kRowsPerWarp;
-    size_t row_off[2 * kRowsPerWarp];
-#pragma unroll
-    for (int r = 0; r < kRowsPerWarp; ++r) {
-      const int f = min(f0 + r, F - 1);
-      row_off[r] = static_cast<size_t>(f) * hv;
-      row_off[kRowsPerWarp + r] = static_cast<size_t>(F + f) * hv;
+  for (int i = threadIdx.x; i < tokens * hv; i += blockDim.x) xs[i] = reinterpret_cast<const uint4*>(x)[i];
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStreamStages; ++s) {
+      mbar_init(&S.full[s], 1);
+      mbar_init(&S.empty[s], kStreamConsumers);
     }
-    const int p_begin = G.start[g], p_end = G.start[g + 1];
-    for (int p0 = p_begin; p0 < p_end; p0 += kTokBatch) {
-      const int nb = min(kTokBatch, p_end - p0);
-      int tok[kTokBatch];
+    S.abort = 0;
+    fence_barrier_init();
+  }
+  build_groups_fused(indices, total, experts, G);  // ends with __syncthreads
+  const int n_groups = G.n_groups;
+  if (threadIdx.x == 0) {
+    int a1 = 0, a2 = 0;
+    for (int g = 0; g < n_groups; ++g) {
+      const int n = G.start[g + 1] - G.start[g];
+      S.batch1_prefix[g] = a1;
+      S.batch2_prefix[g] = a2;
+      a1 += (n + kTokBatch - 1) / kTokBatch;
+      a2 += (n + plan.b2 - 1) / plan.b2;
+    }
+    S.batch1_prefix[n_groups] = a1;
+    S.batch2_prefix[n_groups] = a2;
+  }
+  __syncthreads();
+  const int units1 = S.batch1_prefix[n_groups] * plan.nfr;
+  const int units2 = S.batch2_prefix[n_groups] * plan.nhr;
+  int stage = 0;
+  uint32_t phase = 0;
+  auto advance = [&]() {
+    if (++stage == kStreamStages) {
+      stage = 0;
+      phase ^= 1u;
+    }
+  };
+  const size_t row1 = static_cast<size_t>(H) * 2;  // bytes of one gate/up row
+  const size_t row2 = static_cast<size_t>(F) * 2;  // bytes of one down row
+
+  // ------------------------------------------------------------ phase 1
+  if (warp == kStreamConsumers) {
+    if (lane == 0) {
+      for (int u = blockIdx.x; u < units1; u += gridDim.x) {
+        const int q = u / plan.nfr, fr = u - q * plan.nfr;
+        const int g = find_group(S.batch1_prefix, n_groups, q);
+        const int e = G.expert[g];
+        const int f0 = fr * plan.r1, r = min(plan.r1, F - f0);
+        if (!mbar_wait_bounded(&S.empty[stage], phase ^ 1u, status, kStatusTimeoutProducer, abort_flag)) break;
+        uint8_t* dst = ring + stage * kStreamStageBytes;
+        mbar_arrive_expect_tx(&S.full[stage], static_cast<uint32_t>(2 * r * row1));
+        const uint8_t* base = reinterpret_cast<const uint8_t*>(w1) + (static_cast<size_t>(e) * 2 * F) * row1;
+        bulk_copy_g2s(dst, base + f0 * row1, static_cast<uint32_t>(r * row1), &S.full[stage]);
+        bulk_copy_g2s(dst + plan.r1 * row1, base + (F + f0) * row1, static_cast<uint32_t>(r * row1), &S.full[stage]);
+        advance();
+      }
+    }
+  } else {
+    for (int u = blockIdx.x; u < units1; u += gridDim.x) {
+      const int q = u / plan.nfr, fr = u - q * plan.nfr;
+      const int g = find_group(S.batch1_prefix, n_groups, q);
+      const int batch = q - S.batch1_prefix[g];
+      const int p0 = G.start[g] + batch * kTokBatch;
+      const int nb = min(kTokBatch, G.start[g + 1] - p0);
+      const int f0 = fr * plan.r1, r = min(plan.r1, F - f0);
+      if (!mbar_wait_bounded(&S.full[stage], phase, status, kStatusTimeoutOther, abort_flag)) break;
+      const uint8_t* st = ring + stage * kStreamStageBytes;
+      for (int fl = warp; fl < r; fl += kStreamConsumers) {
+        const uint4* rg = reinterpret_cast<const uint4*>(st + fl * row1);
+        const uint4* ru = reinterpret_cast<const uint4*>(st + (plan.r1 + fl) * row1);
+        int tok[kTokBatch];
 #pragma unroll
-      for (int b = 0; b < kTokBatch; ++b) tok[b] = b < nb ? G.list[p0 + b] / topk : 0;
-      float acc[2 * kRowsPerWarp][kTokBatch];
+        for (int b = 0; b < kTokBatch; ++b) tok[b] = b < nb ? G.list[p0 + b] / topk : 0;
+        float ag[kTokBatch], au[kTokBatch];
 #pragma unroll
-      for (int r = 0; r < 2 * kRowsPerWarp; ++r)
+        for (int b = 0; b < kTokBatch; ++b) ag[b] = au[b] = 0.f;
+        for (int v = lane; v < hv; v += 32) {
+          float wg[8], wu[8];
+          bf16x8_to_f32(rg[v], wg);
+          bf16x8_to_f32(ru[v], wu);
 #pragma unroll
-        for (int b = 0; b < kTokBatch; ++b) acc[r][b] = 0.f;
-#pragma unroll 2
-      for (int v = lane; v < hv; v += 32) {
-        uint4 wv[2 * kRowsPerWarp];
+          for (int b = 0; b < kTokBatch; ++b) {
+            if (b < nb) {
+              float xf[8];
+              bf16x8_to_f32(xs[tok[b] * hv + v], xf);
 #pragma unroll
-        for (int r = 0; r < 2 * kRowsPerWarp; ++r) wv[r] = __ldg(wg + row_off[r] + v);
-        float wf[2 * kRowsPerWarp][8];
-#pragma unroll
-        for (int r = 0; r < 2 * kRowsPerWarp; ++r) bf16x8_to_f32(wv[r], wf[r]);
+              for (int i = 0; i < 8; ++i) {
+                ag[b] = fmaf(wg[i], xf[i], ag[b]);
+                au[b] = fmaf(wu[i], xf[i], au[b]);
+              }
+            }
+          }
+        }
 #pragma unroll
         for (int b = 0; b < kTokBatch; ++b) {
           if (b < nb) {
-            float xf[8];
-            bf16x8_to_f32(xs[tok[b] * hv + v], xf);
-#pragma unroll
-            for (int r = 0; r < 2 * kRowsPerWarp; ++r)
-#pragma unroll
-              for (int i = 0; i < 8; ++i) acc[r][b] = fmaf(wf[r][i], xf[i], acc[r][b]);
+            const float gs = warp_sum(ag[b]);
+            const float us = warp_sum(au[b]);
+            if (lane == 0) glu[static_cast<size_t>(G.list[p0 + b]) * F + f0 + fl] = act_linear(gs, us);
           }
         }
       }
-#pragma unroll
-      for (int b = 0; b < kTokBatch; ++b) {
-        if (b < nb) {
-#pragma unroll
-          for (int r = 0; r < kRowsPerWarp; ++r) {
-            const float gsum = warp_sum(acc[r][b]);
-            const float usum = warp_sum(acc[kRowsPerWarp + r][b]);
-            const int f = f0 + r;
-            if (lane == 0 && f < F) glu[static_cast<size_t>(G.list[p0 + b]) * F + f] = act_linear(gsum, usum);
-          }
-        }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&S.empty[stage]);
+      advance();
+    }
+    fence_proxy_async_global();  // glu stores -> other CTAs' bulk copies after the barrier
+  }
+  if (!grid_barrier_bounded(barrier, gridDim.x, status, kStatusTimeoutOther, &G.flag)) return;
+  if (*abort_flag) return;
+
+  // ------------------------------------------------------------ phase 2
+  if (warp == kStreamConsumers) {
+    if (lane == 0) {
+      fence_proxy_async_global();
+      for (int u = blockIdx.x; u < units2; u += gridDim.x) {
+        const int q = u / plan.nhr, hr = u - q * plan.nhr;
+        const int g = find_group(S.batch2_prefix, n_groups, q);
+        const int batch = q - S.batch2_prefix[g];
+        const int p0 = G.start[g] + batch * plan.b2;
+        const int nb = min(plan.b2, G.start[g + 1] - p0);
+        const int e = G.expert[g];
+        const int h0 = hr * plan.r2, r = min(plan.r2, H - h0);
+        if (!mbar_wait_bounded(&S.empty[stage], phase ^ 1u, status, kStatusTimeoutProducer, abort_flag)) break;
+        uint8_t* dst = ring + stage * kStreamStageBytes;
+        mbar_arrive_expect_tx(&S.full[stage], static_cast<uint32_t>(r * row2 + nb * F * 4));
+        bulk_copy_g2s(dst, reinterpret_cast<const uint8_t*>(w2) + (static_cast<size_t>(e) * H + h0) * row2,
+                      static_cast<uint32_t>(r * row2), &S.full[stage]);
+        for (int b = 0; b < nb; ++b)
+          bulk_copy_g2s(dst + plan.r2 * row2 + static_cast<size_t>(b) * F * 4,
+                        glu + static_cast<size_t>(G.list[p0 + b]) * F, static_cast<uint32_t>(F * 4), &S.full[stage]);
+        advance();
       }
     }
+  } else {
+    for (int u = blockIdx.x; u < units2; u += gridDim.x) {
+      const int q = u / plan.nhr, hr = u - q * plan.nhr;
+      const int g = find_group(S.batch2_prefix, n_groups, q);
+      const int batch = q - S.batch2_prefix[g];
+      const int p0 = G.start[g] + batch * plan.b2;
+      const int nb = min(plan.b2, G.start[g + 1] - p0);
+      const int h0 = hr * plan.r2, r = min(plan.r2, H - h0);
+      if (!mbar_wait_bounded(&S.full[stage], phase, status, kStatusTimeoutOther, abort_flag)) break;
+      const uint8_t* st = ring + stage * kStreamStageBytes;
+      const float4* gl = reinterpret_cast<const float4*>(st + plan.r2 * row2);
+      for (int rr = warp; rr < r; rr += kStreamConsumers) {
+        const uint4* wr = reinterpret_cast<const uint4*>(st + rr * row2);
+        float acc[kTokBatch];
+#pragma unroll
+        for (int b = 0; b < kTokBatch; ++b) acc[b] = 0.f;
+        for (int v = lane; v < fv; v += 32) {
+          float wf[8];
+          bf16x8_to_f32(wr[v], wf);
+#pragma unroll
+          for (int b = 0; b < kTokBatch; ++b) {
+            if (b < nb) {
+              const float4 ga = gl[b * (F / 4) + 2 * v];
+              const float4 gb = gl[b * (F / 4) + 2 * v + 1];
+              acc[b] = fmaf(wf[0], ga.x, acc[b]);
+              acc[b] = fmaf(wf[1], ga.y, acc[b]);
+              acc[b] = fmaf(wf[2], ga.z, acc[b]);
+              acc[b] = fmaf(wf[3], ga.w, acc[b]);
+              acc[b] = fmaf(wf[4], gb.x, acc[b]);
+              acc[b] = fmaf(wf[5], gb.y, acc[b]);
+              acc[b] = fmaf(wf[6], gb.z, acc[b]);
+              acc[b] = fmaf(wf[7], gb.w, acc[b]);
+            }
+          }
+        }
+#pragma unroll
+        for (int b = 0; b < kTokBatch; ++b) {
+          if (b < nb) {
+            const float sum = warp_sum(acc[b]);
+            if (lane == 0) partial[static_cast<size_t>(G.list[p0 + b]) * H + h0 + rr] = sum;
+          }
+        }
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&S.empty[stage]);
+      advance();
+    }
   }
-
   if (!grid_barrier_bounded(barrier, gridDim.x, status, kStatusTimeoutOther, &G.flag)) return;
 
-  // ---- phase 2: down -> partial[pair, h]; last unit of an h-block combines it
-  const int nhb = (H + kRowsPerCta - 1) / kRowsPerCta;
-  float4* gs = reinterpret_cast<float4*>(buf);  // [kTokBatch, F/4] (reuses the x area)
-  if (n_groups == 0) {
-    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < tokens * H; i += gridDim.x * blockDim.x)
-      out[i] = __float2bfloat16_rn(0.f);
-    return;
-  }
-  for (int u = blockIdx.x; u < n_groups * nhb; u += gridDim.x) {
-    const int g = u / nhb, hb = u - (u / nhb) * nhb;
-    const uint4* wd = reinterpret_cast<const uint4*>(w2 + static_cast<size_t>(G.expert[g]) * H * F);
-    const int h0 = hb * kRowsPerCta + warp * kRowsPerWarp;
-    size_t row_off[kRowsPerWarp];
-#pragma unroll
-    for (int r = 0; r < kRowsPerWarp; ++r) row_off[r] = static_cast<size_t>(min(h0 + r, H - 1)) * fv;
-    const int p_begin = G.start[g], p_end = G.start[g + 1];
-    for (int p0 = p_begin; p0 < p_end; p0 += kTokBatch) {
-      const int nb = min(kTokBatch, p_end - p0);
-      __syncthreads();
-      for (int i = threadIdx.x; i < nb * (F / 4); i += blockDim.x) {
-        const int r = i / (F / 4), v = i - r * (F / 4);
-        gs[r * (F / 4) + v] = __ldcg(reinterpret_cast<const float4*>(glu + static_cast<size_t>(G.list[p0 + r]) * F) + v);
-      }
-      __syncthreads();
-      float acc[kRowsPerWarp][kTokBatch];
-#pragma unroll
-      for (int r = 0; r < kRowsPerWarp; ++r)
-#pragma unroll
-        for (int b = 0; b < kTokBatch; ++b) acc[r][b] = 0.f;
-#pragma unroll 4
-      for (int v = lane; v < fv; v += 32) {
-        float wf[kRowsPerWarp][8];
-#pragma unroll
-        for (int r = 0; r < kRowsPerWarp; ++r) bf16x8_to_f32(__ldg(wd + row_off[r] + v), wf[r]);
-#pragma unroll
-        for (int b = 0; b < kTokBatch; ++b) {
-          if (b < nb) {
-            const float4 ga = gs[b * (F / 4) + 2 * v];
-            const float4 gb = gs[b * (F / 4) + 2 * v + 1];
-            const float gf[8] = {ga.x, ga.y, ga.z, ga.w, gb.x, gb.y, gb.z, gb.w};
-#pragma unroll
-            for (int r = 0; r < kRowsPerWarp; ++r)
-#pragma unroll
-              for (int i = 0; i < 8; ++i) acc[r][b] = fmaf(wf[r][i], gf[i], acc[r][b]);
-          }
-        }
-      }
-#pragma unroll
-      for (int b = 0; b < kTokBatch; ++b) {
-        if (b < nb) {
-#pragma unroll
-          for (int r = 0; r < kRowsPerWarp; ++r) {
-            const float sum = warp_sum(acc[r][b]);
-            if (lane == 0 && h0 + r < H) partial[static_cast<size_t>(G.list[p0 + b]) * H + h0 + r] = sum;
-          }
-        }
-      }
+  // ------------------------------------------------------------ phase 3: combine
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < tokens * H; i += gridDim.x * blockDim.x) {
+    const int t = i / H, c = i - t * H;
+    float s = 0.f;
+    for (int j = 0; j < topk; ++j) {
+      const int p = t * topk + j;
+      const int e = indices[p];
+      if (e < 0 || e >= experts) continue;
+      s = fmaf(weights[p], __ldcg(partial + static_cast<size_t>(p) * H + c), s);
     }
-    // arrival on this h-block; the last of the n_groups units combines it
-    __threadfence();
-    __syncthreads();
-    if (threadIdx.x == 0) G.flag = atomicAdd(&counters[hb], 1) == n_groups - 1;
-    __syncthreads();
-    if (G.flag) {
-      __threadfence();
-      const int c0 = hb * kRowsPerCta, c1 = min(H, c0 + kRowsPerCta), width = c1 - c0;
-      for (int i = threadIdx.x; i < tokens * width; i += blockDim.x) {
-        const int t = i / width, c = c0 + (i - t * width);
-        float s = 0.f;
-        for (int j = 0; j < topk; ++j) {
-          const int p = t * topk + j;
-          const int e = indices[p];
-          if (e < 0 || e >= experts) continue;
-          s = fmaf(weights[p], __ldcg(partial + static_cast<size_t>(p) * H + c), s);
-        }
-        out[static_cast<size_t>(t) * H + c] = __float2bfloat16_rn(s);
-      }
-    }
+    out[i] = __float2bfloat16_rn(s);
   }
 }
 
@@ -752,30 +857,30 @@ cudaError_t launch_decode(const DecodeArgs& a, const DecodeWorkspace& ws, cudaSt
   const int H = a.hidden, F = a.inter;
   cudaError_t err;
   if (a.layout == CERNELS_LAYOUT_LINEAR && total <= kFusedMaxPairs) {
-    const size_t operand = std::max(static_cast<size_t>(a.tokens) * H * 2, static_cast<size_t>(kTokBatch) * F * 4);
-    const size_t smem = ((sizeof(FusedGroups) + 15) & ~size_t(15)) + operand;
-    if (smem <= 200 * 1024) {
-      static int attr_smem = 0;
-      if (static_cast<int>(smem) > attr_smem) {
-        if ((err = cudaFuncSetAttribute(decode_fused_linear, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                        200 * 1024)) != cudaSuccess)
+    const StreamPlan plan = make_stream_plan(H, F);
+    const size_t xbytes = static_cast<size_t>(a.tokens) * H * 2;
+    const size_t smem = ((sizeof(StreamShared) + 127) & ~size_t(127)) +
+                        static_cast<size_t>(kStreamStages) * kStreamStageBytes + xbytes;
+    if (plan.r1 > 0 && plan.r2 > 0 && smem <= 220 * 1024) {
+      static bool attr_done = false;
+      if (!attr_done) {
+        if ((err = cudaFuncSetAttribute(decode_stream_linear, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                        220 * 1024)) != cudaSuccess)
           return err;
-        attr_smem = 200 * 1024;
+        attr_done = true;
       }
       int per_sm = 0;
-      if ((err = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, decode_fused_linear, kDecThreads, smem)) !=
-          cudaSuccess)
+      if ((err = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, decode_stream_linear, kStreamThreads,
+                                                                smem)) != cudaSuccess)
         return err;
-      const int n_hblocks = (H + kRowsPerCta - 1) / kRowsPerCta;
-      const int n_fblocks = (F + kRowsPerCta - 1) / kRowsPerCta;
-      const int units = max_groups * std::max(n_hblocks, n_fblocks);
+      const int units = max_groups * std::max(plan.nfr, plan.nhr);
       int grid = std::min(per_sm * device_sm_count(), units);
       if (grid < 1) grid = 1;
-      // arrival counters [n_hblocks] and the grid barrier [2] start at zero
-      if ((err = cudaMemsetAsync(ws.counters, 0, (n_hblocks + 2) * sizeof(int), stream)) != cudaSuccess) return err;
+      // grid barrier words start at zero
+      if ((err = cudaMemsetAsync(ws.counters, 0, 2 * sizeof(int), stream)) != cudaSuccess) return err;
       cudaLaunchConfig_t cfg = {};
       cfg.gridDim = dim3(grid);
-      cfg.blockDim = dim3(kDecThreads);
+      cfg.blockDim = dim3(kStreamThreads);
       cfg.dynamicSmemBytes = smem;
       cfg.stream = stream;
       cudaLaunchAttribute attr[1];
@@ -783,9 +888,9 @@ cudaError_t launch_decode(const DecodeArgs& a, const DecodeWorkspace& ws, cudaSt
       attr[0].val.cooperative = 1;
       cfg.attrs = attr;
       cfg.numAttrs = 1;
-      err = cudaLaunchKernelEx(&cfg, decode_fused_linear, a.x, a.w1, a.w2, a.indices, a.weights, a.tokens, a.topk,
-                               a.experts, H, F, ws.glu, ws.partial, ws.counters,
-                               reinterpret_cast<unsigned*>(ws.counters + n_hblocks), ws.status, a.out);
+      err = cudaLaunchKernelEx(&cfg, decode_stream_linear, a.x, a.w1, a.w2, a.indices, a.weights, a.tokens, a.topk,
+                               a.experts, H, F, ws.glu, ws.partial, reinterpret_cast<unsigned*>(ws.counters),
+                               ws.status, a.out);
       if (err != cudaSuccess) return err;
       return cudaGetLastError();
     }

@@ -203,3 +203,19 @@ __host__ __device__ constexpr uint32_t make_idesc_bf16(int M, int N, int a_mn, i
 }
 
 }  // namespace cernels
+
+namespace cernels {
+// 1-D bulk copy global -> this CTA's shared memory, completion counted on `bar`
+// (both addresses 16-byte aligned, size a multiple of 16). No multicast.
+__device__ __forceinline__ void bulk_copy_g2s(void* dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   smem_u32(dst)),
+               "l"(src), "r"(bytes), "r"(smem_u32(bar))
+               : "memory");
+}
+
+// Orders this thread's generic-proxy global accesses with later async-proxy (bulk copy) ones.
+__device__ __forceinline__ void fence_proxy_async_global() {
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+}  // namespace cernels
