@@ -489,6 +489,7 @@ struct FusedGroups {
   int start[kFusedMaxPairs + 1];
   int count[kFusedMaxPairs];
   int list[kFusedMaxPairs];
+  int eidx[kFusedMaxPairs];
   int word_prefix[kBitmapWords];
   unsigned bitmap[kBitmapWords];
   int flag;
@@ -540,13 +541,17 @@ __device__ void build_groups_fused(const int32_t* __restrict__ indices, int tota
     G.start[G.n_groups] = acc;
   }
   __syncthreads();
-  // Order inside a group does not affect results: each pair's row is computed by the same
-  // lanes in the same order whatever its batch slot.
+  // Pairs of a group in flat order. Every CTA must build the identical list: token batches
+  // of one group are split across CTAs by position in this list.
+  for (int i = threadIdx.x; i < total; i += blockDim.x) G.eidx[i] = indices[i];
+  __syncthreads();
   for (int i = threadIdx.x; i < total; i += blockDim.x) {
-    const int e = indices[i];
+    const int e = G.eidx[i];
     if (e < 0 || e >= experts) continue;
     const int g = G.word_prefix[e >> 5] + __popc(G.bitmap[e >> 5] & ((1u << (e & 31)) - 1u));
-    G.list[G.start[g] + atomicAdd(&G.count[g], 1)] = i;
+    int before = 0;
+    for (int j = 0; j < i; ++j) before += G.eidx[j] == e;
+    G.list[G.start[g] + before] = i;
   }
   __syncthreads();
 }
