@@ -536,7 +536,6 @@ __device__ void build_groups_fused(const int32_t* __restrict__ indices, int tota
     for (int g = 0; g < G.n_groups; ++g) {
       G.start[g] = acc;
       acc += G.count[g];
-      G.count[g] = 0;  // reused as fill cursor
     }
     G.start[G.n_groups] = acc;
   }
