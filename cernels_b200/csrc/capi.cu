@@ -51,7 +51,7 @@ DecodeWorkspace carve_decode(const cernels_moe_shape& s, void* base, F&& done) {
   const size_t tk = static_cast<size_t>(s.tokens) * s.topk;
   DecodeWorkspace w;
   w.status = c.take<int>(1);
-  w.counters = c.take<int>(static_cast<size_t>(s.hidden) / 16 + 8);
+  w.counters = c.take<int>(static_cast<size_t>(s.hidden) + 8);
   w.glu = c.take<float>(tk * s.intermediate + 4);
   w.partial = c.take<float>(tk * s.hidden + 4);
   done(c.off);

@@ -475,12 +475,9 @@ __global__ void __launch_bounds__(kDecThreads) decode_down_gptoss(
                scratch + 3);
 }
 
-// ---------------------------------------------------------------- fused persistent LINEAR decode
-// One cooperative launch: every CTA builds the expert grouping once, then loops over
-// (group, 16-row block) units of the gate/up stage, crosses a bounded grid barrier, and
-// loops over (group, 16-row block) units of the down stage; the last unit to finish an
-// output block combines it (fixed slot order). Requires T * H * 2 and 8 * F * 4 bytes of
-// shared memory (x rows of all tokens, then one batch of fp32 activation rows).
+// ---------------------------------------------------------------- grouping for the streaming kernel
+// Every CTA of the streaming decode kernel builds the same grouping of the (token, slot)
+// pairs by touched expert, in shared memory, at most kFusedMaxPairs pairs.
 constexpr int kFusedMaxPairs = 256;
 
 struct FusedGroups {
@@ -572,7 +569,6 @@ __device__ bool grid_barrier_bounded(unsigned* bar, unsigned n_blocks, int* stat
     } else {
       const unsigned long long t0 = global_timer_ns_dec();
       while (*vgen == gen) {
-        __nanosleep(64);
         if (global_timer_ns_dec() - t0 > kBarrierLimitNs) {
           if (status) atomicCAS(status, 0, code);
           *flag = 0;
@@ -586,49 +582,51 @@ __device__ bool grid_barrier_bounded(unsigned* bar, unsigned n_blocks, int* stat
   return *flag != 0;
 }
 
-// ---------------------------------------------------------------- streaming LINEAR decode
-// One cooperative launch, one CTA per SM, 9 warps. Warp 8 (one lane) streams weight rows
-// with cp.async.bulk into a ring of kStreamStages x kStreamStageBytes of shared memory
-// (completion counted on mbarriers), so ~144 KB per SM are in flight without occupying
-// registers; warps 0-7 compute from shared memory. Each CTA builds the expert grouping
-// once, then:
-//   phase 1  units (group, token batch of <= 8, R1 gate/up row pairs): glu[pair, f] fp32
-//   barrier  (bounded, grid-wide)
-//   phase 2  units (group, token batch of <= B2, R2 down rows); the stage also carries
-//            the batch's fp32 glu rows: partial[pair, h] fp32
-//   barrier
-//   phase 3  out[t, h] = bf16(sum_j w[t, j] * partial[(t, j), h]) in slot order
-constexpr int kStreamStages = 3;
-constexpr int kStreamStageBytes = 48 * 1024;
+#ifndef CERNELS_STREAM_STAGES
+#define CERNELS_STREAM_STAGES 3
+#define CERNELS_STREAM_STAGE_KB 48
+#endif
+constexpr int kStreamStages = CERNELS_STREAM_STAGES;
+constexpr int kStreamStageBytes = CERNELS_STREAM_STAGE_KB * 1024;
 constexpr int kStreamConsumers = 8;
 constexpr int kStreamThreads = (kStreamConsumers + 1) * 32;
+constexpr int kStreamCThreads = kStreamConsumers * 32;  // consumer threads
+constexpr int kStreamMaxR1 = 8;                          // gate/up pairs per stage
+constexpr int kStreamMaxR2 = 16;                         // down rows per stage
+constexpr int kStreamMaxPairs = 12;
+constexpr size_t kL2PrefetchBudget = size_t(64) << 20;    // bytes of down rows prefetched into L2
+
+#ifdef CERNELS_DECODE_TRACE
+// Debug builds only: %globaltimer stamps at phase boundaries, per CTA (thread 0).
+__device__ unsigned long long g_decode_trace[1024][8];
+#define DECODE_TRACE(slot) \
+  if (threadIdx.x == 0 && blockIdx.x < 1024) g_decode_trace[blockIdx.x][slot] = global_timer_ns_dec();
+#else
+#define DECODE_TRACE(slot)
+#endif
 
 struct StreamPlan {
-  int r1, nfr;       // phase 1: f rows per stage, stages per (group, batch)
-  int b2, r2, nhr;   // phase 2: tokens per batch, h rows per stage, stages per (group, batch)
+  int r1, nfr;  // phase 1: gate/up row pairs per stage, stages per (group, token batch)
+  int r2, nhr;  // phase 2: down rows per stage, stages per (group, token batch)
 };
 
 __host__ __device__ inline StreamPlan make_stream_plan(int H, int F) {
   StreamPlan p;
   p.r1 = kStreamStageBytes / (4 * H);
-  if (p.r1 > kStreamConsumers) p.r1 = kStreamConsumers;
+  if (p.r1 > kStreamMaxR1) p.r1 = kStreamMaxR1;
   p.nfr = p.r1 > 0 ? (F + p.r1 - 1) / p.r1 : 0;
-  // Tokens per phase-2 batch: as many as fit next to 8 down rows, at least one.
-  p.b2 = (kStreamStageBytes - 8 * 2 * F) / (4 * F);
-  if (p.b2 < 1) p.b2 = (kStreamStageBytes - 2 * F) / (4 * F) > 0 ? 1 : 0;
-  if (p.b2 > kTokBatch) p.b2 = kTokBatch;
-  p.r2 = p.b2 > 0 ? (kStreamStageBytes - p.b2 * 4 * F) / (2 * F) : 0;
-  if (p.r2 > 4 * kStreamConsumers) p.r2 = 4 * kStreamConsumers;
+  p.r2 = kStreamStageBytes / (2 * F);
+  if (p.r2 > kStreamMaxR2) p.r2 = kStreamMaxR2;
   p.nhr = p.r2 > 0 ? (H + p.r2 - 1) / p.r2 : 0;
   return p;
 }
 
 struct StreamShared {
   FusedGroups G;
-  int batch1_prefix[kFusedMaxPairs + 1];  // phase-1 token batches before group g
-  int batch2_prefix[kFusedMaxPairs + 1];
+  int batch_prefix[kFusedMaxPairs + 1];  // token batches (of <= kTokBatch) before group g
   uint64_t full[kStreamStages];
   uint64_t empty[kStreamStages];
+  float red[kStreamConsumers][2 * kStreamMaxR1 > kStreamMaxR2 ? 2 * kStreamMaxR1 : kStreamMaxR2];
   int abort;
 };
 
@@ -641,6 +639,78 @@ __device__ __forceinline__ int find_group(const int* prefix, int n_groups, int q
   return lo;
 }
 
+// Consumer-warps-only barrier (named barrier 1; the producer warp does not take part).
+__device__ __forceinline__ void consumers_sync() {
+  asm volatile("bar.sync 1, %0;" ::"n"(kStreamConsumers * 32) : "memory");
+}
+
+
+// Reduces 16 per-lane values over the warp with 16 shuffles (transposing butterfly).
+// On return, v[0] of every even lane l holds the warp-wide sum of row
+// 8*bit4(l) + 4*bit3(l) + 2*bit2(l) + bit1(l).
+__device__ __forceinline__ void warp_reduce16(float (&v)[16], int lane) {
+#pragma unroll
+  for (int i = 0; i < 8; ++i) {
+    const bool hi = lane & 16;
+    const float send = hi ? v[i] : v[i + 8];
+    const float keep = hi ? v[i + 8] : v[i];
+    v[i] = keep + __shfl_xor_sync(0xffffffffu, send, 16);
+  }
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const bool hi = lane & 8;
+    const float send = hi ? v[i] : v[i + 4];
+    const float keep = hi ? v[i + 4] : v[i];
+    v[i] = keep + __shfl_xor_sync(0xffffffffu, send, 8);
+  }
+#pragma unroll
+  for (int i = 0; i < 2; ++i) {
+    const bool hi = lane & 4;
+    const float send = hi ? v[i] : v[i + 2];
+    const float keep = hi ? v[i + 2] : v[i];
+    v[i] = keep + __shfl_xor_sync(0xffffffffu, send, 4);
+  }
+  {
+    const bool hi = lane & 2;
+    const float send = hi ? v[0] : v[1];
+    const float keep = hi ? v[1] : v[0];
+    v[0] = keep + __shfl_xor_sync(0xffffffffu, send, 2);
+  }
+  v[0] += __shfl_xor_sync(0xffffffffu, v[0], 1);
+}
+
+struct UnitCoord {
+  int g, p0, nb, r0, rows;
+};
+
+__device__ __forceinline__ UnitCoord unit_coord(const StreamShared& S, int u, int per_batch, int rows_per_unit,
+                                                int rows_total, int n_groups) {
+  const FusedGroups& G = S.G;
+  UnitCoord c;
+  const int q = u / per_batch, r = u - q * per_batch;
+  c.g = find_group(S.batch_prefix, n_groups, q);
+  c.p0 = G.start[c.g] + (q - S.batch_prefix[c.g]) * kTokBatch;
+  c.nb = min(kTokBatch, G.start[c.g + 1] - c.p0);
+  c.r0 = r * rows_per_unit;
+  c.rows = min(rows_per_unit, rows_total - c.r0);
+  return c;
+}
+
+// Streaming LINEAR decode: one cooperative launch, one CTA per SM, 9 warps. Warp 8 (one
+// lane) streams weight rows with cp.async.bulk into a ring of kStreamStages x
+// kStreamStageBytes of shared memory (mbarrier completion); warps 0-7 compute from shared
+// memory. Phase-1 units are grid-strided (all SMs sweep neighbouring rows together);
+// each CTA owns a contiguous range of phase-2 units, so its glu batch rarely changes.
+//   phase 1  units (group, token batch <= 8, r1 gate/up row pairs) -> glu[pair, f] fp32
+//   barrier  (bounded, grid-wide); the producer has already queued its first phase-2
+//            weight stages, which do not depend on phase 1
+//            (and, when they fit in L2, has prefetched its share of them into L2)
+//   phase 2  units (group, token batch, r2 down rows); the batch's fp32 glu rows sit in a
+//            per-CTA buffer reloaded when the unit's (group, batch) changes -> partial[pair, h];
+//            the last unit to finish a row chunk (arrival counter) writes
+//            out[t, h] = bf16(sum_j w[t, j] * partial[(t, j), h]) for it, in slot order j
+// Every stage is split over all 256 consumer threads by columns (each thread owns 16-byte
+// vectors of every row in the stage), then reduced per row with shuffles + shared memory.
 __global__ void __launch_bounds__(kStreamThreads, 1) decode_stream_linear(
     const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ w1, const __nv_bfloat16* __restrict__ w2,
     const int32_t* __restrict__ indices, const float* __restrict__ weights, int tokens, int topk, int experts, int H,
@@ -649,15 +719,18 @@ __global__ void __launch_bounds__(kStreamThreads, 1) decode_stream_linear(
   extern __shared__ __align__(128) uint8_t dsm_raw[];
   StreamShared& S = *reinterpret_cast<StreamShared*>(dsm_raw);
   uint8_t* ring = dsm_raw + ((sizeof(StreamShared) + 127) & ~size_t(127));
-  uint4* xs = reinterpret_cast<uint4*>(ring + kStreamStages * kStreamStageBytes);  // [tokens, H/8]
+  uint8_t* opnd = ring + kStreamStages * kStreamStageBytes;  // x rows (phase 1) / glu batch (phase 2)
+  uint4* xs = reinterpret_cast<uint4*>(opnd);                 // [tokens, H/8] bf16
+  float4* gls = reinterpret_cast<float4*>(opnd);              // [kTokBatch, F/4] fp32
   FusedGroups& G = S.G;
   const int total = tokens * topk;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int hv = H / 8, fv = F / 8;
   const StreamPlan plan = make_stream_plan(H, F);
   volatile int* abort_flag = &S.abort;
+  int* chunk_count = reinterpret_cast<int*>(barrier + 2);  // [nhr] arrivals per down-row chunk
+  DECODE_TRACE(0);
 
-  for (int i = threadIdx.x; i < tokens * hv; i += blockDim.x) xs[i] = reinterpret_cast<const uint4*>(x)[i];
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStreamStages; ++s) {
       mbar_init(&S.full[s], 1);
@@ -666,23 +739,24 @@ __global__ void __launch_bounds__(kStreamThreads, 1) decode_stream_linear(
     S.abort = 0;
     fence_barrier_init();
   }
+  for (int i = threadIdx.x; i < tokens * hv; i += blockDim.x) xs[i] = reinterpret_cast<const uint4*>(x)[i];
   build_groups_fused(indices, total, experts, G);  // ends with __syncthreads
   const int n_groups = G.n_groups;
   if (threadIdx.x == 0) {
-    int a1 = 0, a2 = 0;
+    int acc = 0;
     for (int g = 0; g < n_groups; ++g) {
-      const int n = G.start[g + 1] - G.start[g];
-      S.batch1_prefix[g] = a1;
-      S.batch2_prefix[g] = a2;
-      a1 += (n + kTokBatch - 1) / kTokBatch;
-      a2 += (n + plan.b2 - 1) / plan.b2;
+      S.batch_prefix[g] = acc;
+      acc += (G.start[g + 1] - G.start[g] + kTokBatch - 1) / kTokBatch;
     }
-    S.batch1_prefix[n_groups] = a1;
-    S.batch2_prefix[n_groups] = a2;
+    S.batch_prefix[n_groups] = acc;
   }
   __syncthreads();
-  const int units1 = S.batch1_prefix[n_groups] * plan.nfr;
-  const int units2 = S.batch2_prefix[n_groups] * plan.nhr;
+  DECODE_TRACE(1);
+  const int n_batches = S.batch_prefix[n_groups];
+  const int units1 = n_batches * plan.nfr, units2 = n_batches * plan.nhr;
+  // contiguous unit ranges per CTA
+  const int u2_begin = static_cast<int>((static_cast<long long>(units2) * blockIdx.x) / gridDim.x);
+  const int u2_end = static_cast<int>((static_cast<long long>(units2) * (blockIdx.x + 1)) / gridDim.x);
   int stage = 0;
   uint32_t phase = 0;
   auto advance = [&]() {
@@ -693,163 +767,204 @@ __global__ void __launch_bounds__(kStreamThreads, 1) decode_stream_linear(
   };
   const size_t row1 = static_cast<size_t>(H) * 2;  // bytes of one gate/up row
   const size_t row2 = static_cast<size_t>(F) * 2;  // bytes of one down row
+  bool ok = true;
 
-  // ------------------------------------------------------------ phase 1
   if (warp == kStreamConsumers) {
+    // ------------------------------------------------------------ producer
+    int prefetched = 0;
     if (lane == 0) {
-      for (int u = blockIdx.x; u < units1; u += gridDim.x) {
-        const int q = u / plan.nfr, fr = u - q * plan.nfr;
-        const int g = find_group(S.batch1_prefix, n_groups, q);
-        const int e = G.expert[g];
-        const int f0 = fr * plan.r1, r = min(plan.r1, F - f0);
-        if (!mbar_wait_bounded(&S.empty[stage], phase ^ 1u, status, kStatusTimeoutProducer, abort_flag)) break;
+      // When this launch's down-projection rows fit comfortably in L2, prefetch this CTA's
+      // share into L2 while phase 1 streams, so HBM stays busy across the grid barrier.
+      const bool prefetch = static_cast<size_t>(units2) * plan.r2 * row2 <= kL2PrefetchBudget;
+      const int n1 = (units1 - static_cast<int>(blockIdx.x) + static_cast<int>(gridDim.x) - 1) / static_cast<int>(gridDim.x);
+      const int n2 = u2_end - u2_begin;
+      int i1 = 0, pf = u2_begin + kStreamStages;  // the first stages are loaded into smem directly
+      for (int u = blockIdx.x; u < units1 && ok; u += gridDim.x, ++i1) {
+        if (prefetch && n1 > 0) {
+          const int pf_end = u2_begin + static_cast<int>((static_cast<long long>(n2) * (i1 + 1)) / n1);
+          for (; pf < pf_end; ++pf) {
+            const UnitCoord c2 = unit_coord(S, pf, plan.nhr, plan.r2, H, n_groups);
+            bulk_prefetch_l2(reinterpret_cast<const uint8_t*>(w2) + (static_cast<size_t>(G.expert[c2.g]) * H + c2.r0) * row2,
+                             static_cast<uint32_t>(c2.rows * row2));
+          }
+        }
+        const UnitCoord c = unit_coord(S, u, plan.nfr, plan.r1, F, n_groups);
+        const int e = G.expert[c.g];
+        if (!mbar_wait_bounded(&S.empty[stage], phase ^ 1u, status, kStatusTimeoutProducer, abort_flag)) {
+          ok = false;
+          break;
+        }
         uint8_t* dst = ring + stage * kStreamStageBytes;
-        mbar_arrive_expect_tx(&S.full[stage], static_cast<uint32_t>(2 * r * row1));
+        mbar_arrive_expect_tx(&S.full[stage], static_cast<uint32_t>(2 * c.rows * row1));
         const uint8_t* base = reinterpret_cast<const uint8_t*>(w1) + (static_cast<size_t>(e) * 2 * F) * row1;
-        bulk_copy_g2s(dst, base + f0 * row1, static_cast<uint32_t>(r * row1), &S.full[stage]);
-        bulk_copy_g2s(dst + plan.r1 * row1, base + (F + f0) * row1, static_cast<uint32_t>(r * row1), &S.full[stage]);
+        bulk_copy_g2s(dst, base + c.r0 * row1, static_cast<uint32_t>(c.rows * row1), &S.full[stage]);
+        bulk_copy_g2s(dst + plan.r1 * row1, base + (F + c.r0) * row1, static_cast<uint32_t>(c.rows * row1),
+                      &S.full[stage]);
+        advance();
+      }
+      // phase-2 weight rows do not depend on phase 1: queue the first stages now
+      for (int u = u2_begin; u < u2_end && prefetched < kStreamStages && ok; ++u, ++prefetched) {
+        const UnitCoord c = unit_coord(S, u, plan.nhr, plan.r2, H, n_groups);
+        if (!mbar_wait_bounded(&S.empty[stage], phase ^ 1u, status, kStatusTimeoutProducer, abort_flag)) {
+          ok = false;
+          break;
+        }
+        mbar_arrive_expect_tx(&S.full[stage], static_cast<uint32_t>(c.rows * row2));
+        bulk_copy_g2s(ring + stage * kStreamStageBytes,
+                      reinterpret_cast<const uint8_t*>(w2) + (static_cast<size_t>(G.expert[c.g]) * H + c.r0) * row2,
+                      static_cast<uint32_t>(c.rows * row2), &S.full[stage]);
         advance();
       }
     }
-  } else {
-    for (int u = blockIdx.x; u < units1; u += gridDim.x) {
-      const int q = u / plan.nfr, fr = u - q * plan.nfr;
-      const int g = find_group(S.batch1_prefix, n_groups, q);
-      const int batch = q - S.batch1_prefix[g];
-      const int p0 = G.start[g] + batch * kTokBatch;
-      const int nb = min(kTokBatch, G.start[g + 1] - p0);
-      const int f0 = fr * plan.r1, r = min(plan.r1, F - f0);
-      if (!mbar_wait_bounded(&S.full[stage], phase, status, kStatusTimeoutOther, abort_flag)) break;
-      const uint8_t* st = ring + stage * kStreamStageBytes;
-      for (int fl = warp; fl < r; fl += kStreamConsumers) {
-        const uint4* rg = reinterpret_cast<const uint4*>(st + fl * row1);
-        const uint4* ru = reinterpret_cast<const uint4*>(st + (plan.r1 + fl) * row1);
-        int tok[kTokBatch];
-#pragma unroll
-        for (int b = 0; b < kTokBatch; ++b) tok[b] = b < nb ? G.list[p0 + b] / topk : 0;
-        float ag[kTokBatch], au[kTokBatch];
-#pragma unroll
-        for (int b = 0; b < kTokBatch; ++b) ag[b] = au[b] = 0.f;
-        for (int v = lane; v < hv; v += 32) {
-          float wg[8], wu[8];
-          bf16x8_to_f32(rg[v], wg);
-          bf16x8_to_f32(ru[v], wu);
-#pragma unroll
-          for (int b = 0; b < kTokBatch; ++b) {
-            if (b < nb) {
-              float xf[8];
-              bf16x8_to_f32(xs[tok[b] * hv + v], xf);
-#pragma unroll
-              for (int i = 0; i < 8; ++i) {
-                ag[b] = fmaf(wg[i], xf[i], ag[b]);
-                au[b] = fmaf(wu[i], xf[i], au[b]);
-              }
-            }
-          }
-        }
-#pragma unroll
-        for (int b = 0; b < kTokBatch; ++b) {
-          if (b < nb) {
-            const float gs = warp_sum(ag[b]);
-            const float us = warp_sum(au[b]);
-            if (lane == 0) glu[static_cast<size_t>(G.list[p0 + b]) * F + f0 + fl] = act_linear(gs, us);
-          }
-        }
-      }
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&S.empty[stage]);
-      advance();
-    }
-    fence_proxy_async_global();  // glu stores -> other CTAs' bulk copies after the barrier
-  }
-  if (!grid_barrier_bounded(barrier, gridDim.x, status, kStatusTimeoutOther, &G.flag)) return;
-  if (*abort_flag) return;
-
-  // ------------------------------------------------------------ phase 2
-  if (warp == kStreamConsumers) {
-    if (lane == 0) {
-      fence_proxy_async_global();
-      for (int u = blockIdx.x; u < units2; u += gridDim.x) {
-        const int q = u / plan.nhr, hr = u - q * plan.nhr;
-        const int g = find_group(S.batch2_prefix, n_groups, q);
-        const int batch = q - S.batch2_prefix[g];
-        const int p0 = G.start[g] + batch * plan.b2;
-        const int nb = min(plan.b2, G.start[g + 1] - p0);
-        const int e = G.expert[g];
-        const int h0 = hr * plan.r2, r = min(plan.r2, H - h0);
+    if (!grid_barrier_bounded(barrier, gridDim.x, status, kStatusTimeoutOther, &G.flag) || *abort_flag) return;
+    if (lane == 0 && ok) {
+      for (int u = u2_begin + prefetched; u < u2_end; ++u) {
+        const UnitCoord c = unit_coord(S, u, plan.nhr, plan.r2, H, n_groups);
         if (!mbar_wait_bounded(&S.empty[stage], phase ^ 1u, status, kStatusTimeoutProducer, abort_flag)) break;
-        uint8_t* dst = ring + stage * kStreamStageBytes;
-        mbar_arrive_expect_tx(&S.full[stage], static_cast<uint32_t>(r * row2 + nb * F * 4));
-        bulk_copy_g2s(dst, reinterpret_cast<const uint8_t*>(w2) + (static_cast<size_t>(e) * H + h0) * row2,
-                      static_cast<uint32_t>(r * row2), &S.full[stage]);
-        for (int b = 0; b < nb; ++b)
-          bulk_copy_g2s(dst + plan.r2 * row2 + static_cast<size_t>(b) * F * 4,
-                        glu + static_cast<size_t>(G.list[p0 + b]) * F, static_cast<uint32_t>(F * 4), &S.full[stage]);
+        mbar_arrive_expect_tx(&S.full[stage], static_cast<uint32_t>(c.rows * row2));
+        bulk_copy_g2s(ring + stage * kStreamStageBytes,
+                      reinterpret_cast<const uint8_t*>(w2) + (static_cast<size_t>(G.expert[c.g]) * H + c.r0) * row2,
+                      static_cast<uint32_t>(c.rows * row2), &S.full[stage]);
         advance();
       }
     }
   } else {
-    for (int u = blockIdx.x; u < units2; u += gridDim.x) {
-      const int q = u / plan.nhr, hr = u - q * plan.nhr;
-      const int g = find_group(S.batch2_prefix, n_groups, q);
-      const int batch = q - S.batch2_prefix[g];
-      const int p0 = G.start[g] + batch * plan.b2;
-      const int nb = min(plan.b2, G.start[g + 1] - p0);
-      const int h0 = hr * plan.r2, r = min(plan.r2, H - h0);
-      if (!mbar_wait_bounded(&S.full[stage], phase, status, kStatusTimeoutOther, abort_flag)) break;
+    // ------------------------------------------------------------ consumers, phase 1
+    for (int u = blockIdx.x; u < units1; u += gridDim.x) {
+      const UnitCoord c = unit_coord(S, u, plan.nfr, plan.r1, F, n_groups);
+      if (!mbar_wait_bounded(&S.full[stage], phase, status, kStatusTimeoutOther, abort_flag)) {
+        ok = false;
+        break;
+      }
       const uint8_t* st = ring + stage * kStreamStageBytes;
-      const float4* gl = reinterpret_cast<const float4*>(st + plan.r2 * row2);
-      for (int rr = warp; rr < r; rr += kStreamConsumers) {
-        const uint4* wr = reinterpret_cast<const uint4*>(st + rr * row2);
-        float acc[kTokBatch];
+      // All 256 consumer threads split the columns; each owns 16-byte vectors of every
+      // row of the stage (2 * r1 independent FMA chains), then rows are reduced.
+      for (int b = 0; b < c.nb; ++b) {
+        const int pair = G.list[c.p0 + b];
+        const uint4* xrow = xs + static_cast<size_t>(pair / topk) * hv;
+        float acc[2 * kStreamMaxR1];
 #pragma unroll
-        for (int b = 0; b < kTokBatch; ++b) acc[b] = 0.f;
-        for (int v = lane; v < fv; v += 32) {
-          float wf[8];
-          bf16x8_to_f32(wr[v], wf);
+        for (int r = 0; r < 2 * kStreamMaxR1; ++r) acc[r] = 0.f;
+        for (int v = threadIdx.x; v < hv; v += kStreamCThreads) {
+          float xf[8];
+          bf16x8_to_f32(xrow[v], xf);
 #pragma unroll
-          for (int b = 0; b < kTokBatch; ++b) {
-            if (b < nb) {
-              const float4 ga = gl[b * (F / 4) + 2 * v];
-              const float4 gb = gl[b * (F / 4) + 2 * v + 1];
-              acc[b] = fmaf(wf[0], ga.x, acc[b]);
-              acc[b] = fmaf(wf[1], ga.y, acc[b]);
-              acc[b] = fmaf(wf[2], ga.z, acc[b]);
-              acc[b] = fmaf(wf[3], ga.w, acc[b]);
-              acc[b] = fmaf(wf[4], gb.x, acc[b]);
-              acc[b] = fmaf(wf[5], gb.y, acc[b]);
-              acc[b] = fmaf(wf[6], gb.z, acc[b]);
-              acc[b] = fmaf(wf[7], gb.w, acc[b]);
+          for (int r = 0; r < 2 * kStreamMaxR1; ++r) {
+            const int rr = r < kStreamMaxR1 ? r : plan.r1 + (r - kStreamMaxR1);  // gate r / up r
+            if ((r < kStreamMaxR1 ? r : r - kStreamMaxR1) < c.rows) {
+              float wf[8];
+              bf16x8_to_f32(reinterpret_cast<const uint4*>(st + rr * row1)[v], wf);
+#pragma unroll
+              for (int i = 0; i < 8; ++i) acc[r] = fmaf(wf[i], xf[i], acc[r]);
             }
           }
         }
+        warp_reduce16(acc, lane);
+        // row index of this lane's sum: bit 4 -> v[i] vs v[i+8], bit 3 -> +4, bit 2 -> +2, bit 1 -> +1
+        if ((lane & 1) == 0) S.red[warp][((lane >> 4) & 1) * 8 + ((lane >> 3) & 1) * 4 + ((lane >> 2) & 1) * 2 +
+                                          ((lane >> 1) & 1)] = acc[0];
+        consumers_sync();
+        if (threadIdx.x < c.rows) {
+          float gs = 0.f, us = 0.f;
 #pragma unroll
-        for (int b = 0; b < kTokBatch; ++b) {
-          if (b < nb) {
-            const float sum = warp_sum(acc[b]);
-            if (lane == 0) partial[static_cast<size_t>(G.list[p0 + b]) * H + h0 + rr] = sum;
+          for (int w = 0; w < kStreamConsumers; ++w) {
+            gs += S.red[w][threadIdx.x];
+            us += S.red[w][kStreamMaxR1 + threadIdx.x];
           }
+          glu[static_cast<size_t>(pair) * F + c.r0 + threadIdx.x] = act_linear(gs, us);
+        }
+        consumers_sync();
+      }
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&S.empty[stage]);
+      advance();
+    }
+    DECODE_TRACE(2);
+    if (!grid_barrier_bounded(barrier, gridDim.x, status, kStatusTimeoutOther, &G.flag) || *abort_flag) return;
+    DECODE_TRACE(3);
+    // ------------------------------------------------------------ consumers, phase 2
+    int cur_g = -1, cur_p0 = -1;
+    for (int u = u2_begin; u < u2_end && ok; ++u) {
+      const UnitCoord c = unit_coord(S, u, plan.nhr, plan.r2, H, n_groups);
+      if (c.g != cur_g || c.p0 != cur_p0) {  // (group, batch) changed: reload its glu rows
+        consumers_sync();
+        for (int i = threadIdx.x; i < c.nb * (F / 4); i += kStreamConsumers * 32) {
+          const int b = i / (F / 4), v = i - b * (F / 4);
+          gls[b * (F / 4) + v] = __ldcg(reinterpret_cast<const float4*>(glu + static_cast<size_t>(G.list[c.p0 + b]) * F) + v);
+        }
+        consumers_sync();
+        cur_g = c.g;
+        cur_p0 = c.p0;
+      }
+      if (!mbar_wait_bounded(&S.full[stage], phase, status, kStatusTimeoutOther, abort_flag)) break;
+      const uint8_t* st = ring + stage * kStreamStageBytes;
+      for (int b = 0; b < c.nb; ++b) {
+        float acc[kStreamMaxR2];
+#pragma unroll
+        for (int r = 0; r < kStreamMaxR2; ++r) acc[r] = 0.f;
+        for (int v = threadIdx.x; v < fv; v += kStreamCThreads) {
+          const float4 ga = gls[b * (F / 4) + 2 * v];
+          const float4 gb = gls[b * (F / 4) + 2 * v + 1];
+#pragma unroll
+          for (int r = 0; r < kStreamMaxR2; ++r) {
+            if (r < c.rows) {
+              float wf[8];
+              bf16x8_to_f32(reinterpret_cast<const uint4*>(st + r * row2)[v], wf);
+              acc[r] = fmaf(wf[0], ga.x, acc[r]);
+              acc[r] = fmaf(wf[1], ga.y, acc[r]);
+              acc[r] = fmaf(wf[2], ga.z, acc[r]);
+              acc[r] = fmaf(wf[3], ga.w, acc[r]);
+              acc[r] = fmaf(wf[4], gb.x, acc[r]);
+              acc[r] = fmaf(wf[5], gb.y, acc[r]);
+              acc[r] = fmaf(wf[6], gb.z, acc[r]);
+              acc[r] = fmaf(wf[7], gb.w, acc[r]);
+            }
+          }
+        }
+        warp_reduce16(acc, lane);
+        if ((lane & 1) == 0) S.red[warp][((lane >> 4) & 1) * 8 + ((lane >> 3) & 1) * 4 + ((lane >> 2) & 1) * 2 +
+                                          ((lane >> 1) & 1)] = acc[0];
+        consumers_sync();
+        if (threadIdx.x < c.rows) {
+          float sum = 0.f;
+#pragma unroll
+          for (int w = 0; w < kStreamConsumers; ++w) sum += S.red[w][threadIdx.x];
+          partial[static_cast<size_t>(G.list[c.p0 + b]) * H + c.r0 + threadIdx.x] = sum;
+        }
+        consumers_sync();
+      }
+      // Arrival on this row chunk; the last of its n_batches units writes the output rows
+      // (sum over slots j = 0..topk-1 in order, independent of arrival order).
+      const int hr = c.r0 / plan.r2;
+      __threadfence();
+      consumers_sync();
+      if (threadIdx.x == 0) G.flag = atomicAdd(&chunk_count[hr], 1) == n_batches - 1;
+      consumers_sync();
+      if (G.flag) {
+        __threadfence();
+        for (int i = threadIdx.x; i < tokens * c.rows; i += kStreamCThreads) {
+          const int t = i / c.rows, h = c.r0 + (i - t * c.rows);
+          float acc = 0.f;
+          for (int j = 0; j < topk; ++j) {
+            const int p = t * topk + j;
+            const int e = indices[p];
+            if (e < 0 || e >= experts) continue;
+            acc = fmaf(weights[p], __ldcg(partial + static_cast<size_t>(p) * H + h), acc);
+          }
+          out[static_cast<size_t>(t) * H + h] = __float2bfloat16_rn(acc);
         }
       }
       __syncwarp();
       if (lane == 0) mbar_arrive(&S.empty[stage]);
       advance();
     }
+    DECODE_TRACE(4);
   }
-  if (!grid_barrier_bounded(barrier, gridDim.x, status, kStatusTimeoutOther, &G.flag)) return;
-
-  // ------------------------------------------------------------ phase 3: combine
-  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < tokens * H; i += gridDim.x * blockDim.x) {
-    const int t = i / H, c = i - t * H;
-    float s = 0.f;
-    for (int j = 0; j < topk; ++j) {
-      const int p = t * topk + j;
-      const int e = indices[p];
-      if (e < 0 || e >= experts) continue;
-      s = fmaf(weights[p], __ldcg(partial + static_cast<size_t>(p) * H + c), s);
-    }
-    out[i] = __float2bfloat16_rn(s);
-  }
+  // no group at all: every output row is zero
+  if (n_groups == 0)
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < tokens * H; i += gridDim.x * blockDim.x)
+      out[i] = __float2bfloat16_rn(0.f);
+  DECODE_TRACE(6);
 }
 
 }  // namespace
@@ -860,11 +975,13 @@ cudaError_t launch_decode(const DecodeArgs& a, const DecodeWorkspace& ws, cudaSt
   const int max_groups = total < a.experts ? total : a.experts;
   const int H = a.hidden, F = a.inter;
   cudaError_t err;
-  if (a.layout == CERNELS_LAYOUT_LINEAR && total <= kFusedMaxPairs) {
+  // The streaming kernel wins only for a few pairs (each touched expert costs a grid-wide
+  // pass); larger decode batches use the two-kernel path below.
+  if (a.layout == CERNELS_LAYOUT_LINEAR && total <= kStreamMaxPairs) {
     const StreamPlan plan = make_stream_plan(H, F);
-    const size_t xbytes = static_cast<size_t>(a.tokens) * H * 2;
+    const size_t opnd = std::max(static_cast<size_t>(a.tokens) * H * 2, static_cast<size_t>(kTokBatch) * F * 4);
     const size_t smem = ((sizeof(StreamShared) + 127) & ~size_t(127)) +
-                        static_cast<size_t>(kStreamStages) * kStreamStageBytes + xbytes;
+                        static_cast<size_t>(kStreamStages) * kStreamStageBytes + opnd;
     if (plan.r1 > 0 && plan.r2 > 0 && smem <= 220 * 1024) {
       static bool attr_done = false;
       if (!attr_done) {
@@ -880,8 +997,8 @@ cudaError_t launch_decode(const DecodeArgs& a, const DecodeWorkspace& ws, cudaSt
       const int units = max_groups * std::max(plan.nfr, plan.nhr);
       int grid = std::min(per_sm * device_sm_count(), units);
       if (grid < 1) grid = 1;
-      // grid barrier words start at zero
-      if ((err = cudaMemsetAsync(ws.counters, 0, 2 * sizeof(int), stream)) != cudaSuccess) return err;
+      // grid barrier words and the per-chunk arrival counters start at zero
+      if ((err = cudaMemsetAsync(ws.counters, 0, (2 + plan.nhr) * sizeof(int), stream)) != cudaSuccess) return err;
       cudaLaunchConfig_t cfg = {};
       cfg.gridDim = dim3(grid);
       cfg.blockDim = dim3(kStreamThreads);

@@ -219,3 +219,10 @@ __device__ __forceinline__ void fence_proxy_async_global() {
   asm volatile("fence.proxy.async.global;" ::: "memory");
 }
 }  // namespace cernels
+
+namespace cernels {
+// Prefetches [src, src + bytes) from global memory into L2 (size a multiple of 16).
+__device__ __forceinline__ void bulk_prefetch_l2(const void* src, uint32_t bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(src), "r"(bytes) : "memory");
+}
+}  // namespace cernels

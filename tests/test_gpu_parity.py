@@ -155,7 +155,7 @@ def test_empty_batch():
 
 # ---------------------------------------------------------------- decode
 @pytest.mark.parametrize("layout", [LAYOUT_LINEAR, LAYOUT_GPTOSS])
-@pytest.mark.parametrize("T", [1, 2, 4, 8, 33, 60])
+@pytest.mark.parametrize("T", [1, 2, 3, 4, 8, 33, 60])
 def test_decode_matches_oracle_and_prefill(T, layout):
     g = torch.Generator().manual_seed(100 + T)
     H, E, F, k = (2048, 64, 1408, 6) if layout == LAYOUT_LINEAR else (2880, 32, 2880, 4)
