@@ -251,3 +251,20 @@ def test_cuda_graph_capture_and_replay(decode):
         torch.cuda.synchronize()
         eager = fn(x, w1, w2, idx, w, k)
         assert torch.equal(out, eager)
+
+
+@pytest.mark.parametrize("T,H,E,F,k", [(1, 64, 4, 32, 2), (2, 72, 3, 40, 3), (1, 2880, 16, 768, 6), (2, 512, 512, 512, 6),
+                                       (1, 4096, 8, 1536, 4)])
+def test_decode_streaming_shapes(T, H, E, F, k):
+    """Small decode batches (<= 12 pairs) take the bulk-copy streaming kernel."""
+    g = torch.Generator().manual_seed(T * 7 + H)
+    x = torch.randn(T, H, generator=g).to(torch.bfloat16)
+    w1 = (torch.randn(E, 2 * F, H, generator=g) * 0.05).to(torch.bfloat16)
+    w2 = (torch.randn(E, H, F, generator=g) * 0.05).to(torch.bfloat16)
+    idx = torch.stack([torch.randperm(E, generator=g)[:k] for _ in range(T)])
+    idx[0, 0] = -1  # one skipped slot
+    w = torch.rand(T, k, generator=g)
+    out = run_op(x, w1, w2, idx, w, k, LAYOUT_LINEAR, True)
+    assert_close(out, oracle_out(x, w1, w2, idx, w, LAYOUT_LINEAR))
+    none = run_op(x, w1, w2, torch.full_like(idx, -1), w, k, LAYOUT_LINEAR, True)
+    assert torch.count_nonzero(none) == 0
