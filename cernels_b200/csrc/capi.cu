@@ -208,6 +208,7 @@ static int run_prefill(const cernels_moe_shape* shape, const void* x, const void
   g1.k = s.hidden;
   g1.n = 2 * s.intermediate;
   g1.out_cols = s.intermediate;
+  g1.weight_experts = s.experts;
   err = launch_grouped_gemm(gptoss ? kGateUpGptOss : kGateUpLinear, g1, sms, stream);
   if (err != cudaSuccess) return cuda_rc(err);
   mark(3);
@@ -224,6 +225,7 @@ static int run_prefill(const cernels_moe_shape* shape, const void* x, const void
   g2.k = s.intermediate;
   g2.n = s.hidden;
   g2.out_cols = s.hidden;
+  g2.weight_experts = s.experts;
   err = launch_grouped_gemm(gptoss ? kDownGptOss : kDownLinear, g2, sms, stream);
   if (err != cudaSuccess) return cuda_rc(err);
   mark(4);
@@ -290,6 +292,57 @@ int cernels_moe_experts_decode(const cernels_moe_shape* shape, const void* x, co
   a.topk = s.topk;
   a.layout = s.layout;
   return cuda_rc(launch_decode(a, ws, stream));
+}
+
+int cernels_moe_grouped_experts(const cernels_moe_shape* shape, int32_t groups, const int32_t* group_counts,
+                                const void* rows_in, const void* gate_up_proj, const float* gate_up_bias,
+                                const void* down_proj, const float* down_bias, void* rows_out, void* workspace,
+                                size_t workspace_bytes, void* stream_ptr) {
+  int rc = check_shape(shape);
+  if (rc) return rc;
+  const cernels_moe_shape s = *shape;
+  if (groups <= 0 || groups > kMaxExperts || groups % s.experts != 0) return CERNELS_E_INVALID_SHAPE;
+  if (s.tokens == 0) return CERNELS_OK;
+  if (!group_counts || !rows_in || !gate_up_proj || !down_proj || !rows_out) return CERNELS_E_NULL;
+  if (!aligned16(rows_in) || !aligned16(rows_out) || !aligned16(gate_up_proj) || !aligned16(down_proj))
+    return CERNELS_E_ALIGNMENT;
+  cernels_moe_shape ws_shape = s;
+  ws_shape.experts = groups;
+  ws_shape.topk = 1;
+  if (!workspace || workspace_bytes < prefill_workspace_bytes(ws_shape)) return CERNELS_E_WORKSPACE;
+  if ((rc = check_device())) return rc;
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
+  const PrefillWorkspace ws = carve_prefill_workspace(ws_shape, workspace);
+  const bool gptoss = s.layout == CERNELS_LAYOUT_GPTOSS;
+  cudaError_t err = cudaMemsetAsync(ws.status, 0, sizeof(int), stream);
+  if (err == cudaSuccess) err = launch_segments(group_counts, groups, ws.block_counts, ws.offsets, ws.mtile_offsets, stream);
+  if (err != cudaSuccess) return cuda_rc(err);
+  const int sms = device_sm_count();
+  GroupedGemmArgs g1{};
+  g1.a = static_cast<const __nv_bfloat16*>(rows_in);
+  g1.b = static_cast<const __nv_bfloat16*>(gate_up_proj);
+  g1.bias = gptoss ? gate_up_bias : nullptr;
+  g1.out = ws.glu;
+  g1.offsets = ws.offsets;
+  g1.mtile_offsets = ws.mtile_offsets;
+  g1.status = ws.status;
+  g1.rows = s.tokens;
+  g1.experts = groups;
+  g1.k = s.hidden;
+  g1.n = 2 * s.intermediate;
+  g1.out_cols = s.intermediate;
+  g1.weight_experts = s.experts;
+  err = launch_grouped_gemm(gptoss ? kGateUpGptOss : kGateUpLinear, g1, sms, stream);
+  if (err != cudaSuccess) return cuda_rc(err);
+  GroupedGemmArgs g2 = g1;
+  g2.a = ws.glu;
+  g2.b = static_cast<const __nv_bfloat16*>(down_proj);
+  g2.bias = gptoss ? down_bias : nullptr;
+  g2.out = static_cast<__nv_bfloat16*>(rows_out);
+  g2.k = s.intermediate;
+  g2.n = s.hidden;
+  g2.out_cols = s.hidden;
+  return cuda_rc(launch_grouped_gemm(gptoss ? kDownGptOss : kDownLinear, g2, sms, stream));
 }
 
 int cernels_moe_route(const cernels_moe_shape* shape, const int32_t* indices, const float* weights,

@@ -146,6 +146,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x) {
         const TileCoord c = decode_tile(t, n_tiles, s_mt, experts);
         const int row0 = args.offsets[c.expert] + c.m_tile * BM;
+        const int we = c.expert % args.weight_experts;  // weight slab of this row group
         for (int kb = 0; kb < k_blocks; ++kb) {
           if (!mbar_wait_bounded(&empty_bar[stage], phase ^ 1u, args.status, kStatusTimeoutProducer, abort_flag)) {
             ok = false;
@@ -158,17 +159,17 @@ __global__ void __launch_bounds__(kThreads, 1)
           if constexpr (kMode == kGateUpLinear) {
             const int f0 = c.n_tile * 128;
             const int half_f = args.n / 2;
-            tma_load_3d(b_dst, &tmap_b, &full_bar[stage], kb * BK, f0, c.expert, kCacheEvictNormal);
-            tma_load_3d(b_dst + kBBytes / 2, &tmap_b, &full_bar[stage], kb * BK, half_f + f0, c.expert,
+            tma_load_3d(b_dst, &tmap_b, &full_bar[stage], kb * BK, f0, we, kCacheEvictNormal);
+            tma_load_3d(b_dst + kBBytes / 2, &tmap_b, &full_bar[stage], kb * BK, half_f + f0, we,
                         kCacheEvictNormal);
           } else if constexpr (kMode == kDownLinear) {
-            tma_load_3d(b_dst, &tmap_b, &full_bar[stage], kb * BK, c.n_tile * BN, c.expert, kCacheEvictNormal);
+            tma_load_3d(b_dst, &tmap_b, &full_bar[stage], kb * BK, c.n_tile * BN, we, kCacheEvictNormal);
           } else {
             // N-major weights: four 64-column boxes, each [64 K rows x 128 bytes].
 #pragma unroll
             for (int j = 0; j < 4; ++j)
               tma_load_3d(b_dst + j * (kBBytes / 4), &tmap_b, &full_bar[stage], c.n_tile * BN + 64 * j, kb * BK,
-                          c.expert, kCacheEvictNormal);
+                          we, kCacheEvictNormal);
           }
           if (++stage == kStages) {
             stage = 0;
@@ -229,9 +230,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!mbar_wait_bounded(&tfull_bar[acc], acc_phase, args.status, kStatusTimeoutEpilogue, abort_flag)) break;
       tc_fence_after();
       const TileCoord c = decode_tile(t, n_tiles, s_mt, experts);
-      const int e = c.expert;
-      const int row_begin = args.offsets[e];
-      const int rows_e = args.offsets[e + 1] - row_begin;
+      const int e = c.expert % args.weight_experts;  // weight slab (bias row) of this row group
+      const int row_begin = args.offsets[c.expert];
+      const int rows_e = args.offsets[c.expert + 1] - row_begin;
       const int local_row = c.m_tile * BM + quarter * 32 + lane;
       const bool row_ok = local_row < rows_e;
       const size_t grow = static_cast<size_t>(row_begin + local_row);
@@ -351,7 +352,7 @@ cudaError_t launch_mode(const GroupedGemmArgs& args, int num_sms, cudaStream_t s
     const uint32_t box[2] = {BK, BM};
     if (!encode_map(&map_a, args.a, 2, dims, strides, box)) return cudaErrorInvalidValue;
   }
-  const uint64_t E = static_cast<uint64_t>(args.experts);
+  const uint64_t E = static_cast<uint64_t>(args.weight_experts);
   if constexpr (kMode == kGateUpLinear || kMode == kDownLinear) {
     // Weight [E, N, K] (K contiguous): dims (K, N, E).
     const uint64_t dims[3] = {static_cast<uint64_t>(args.k), static_cast<uint64_t>(args.n), E};

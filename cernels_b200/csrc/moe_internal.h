@@ -58,6 +58,10 @@ cudaError_t launch_route(const int32_t* indices, const float* weights, int token
 // Copies rows [0, rows) (and only those below *row_count when row_count is non-null).
 cudaError_t launch_gather(const __nv_bfloat16* x, const int* perm_token, int rows, const int* row_count,
                           int hidden, __nv_bfloat16* gathered, cudaStream_t stream);
+// Row groups given by counts: offsets[g] = sum of counts before g, mtile_offsets likewise in
+// 128-row tiles. `scratch` holds `groups` ints.
+cudaError_t launch_segments(const int* counts, int groups, int* scratch, int* offsets, int* mtile_offsets,
+                            cudaStream_t stream);
 cudaError_t launch_combine(const __nv_bfloat16* down_out, const int* inv, const float* weights, int tokens,
                            int topk, int hidden, __nv_bfloat16* out, cudaStream_t stream);
 
@@ -74,6 +78,7 @@ struct GroupedGemmArgs {
   int k;                       // reduction length
   int n;                       // columns of the weight product (2F or H)
   int out_cols;                // F for gate/up, H for down
+  int weight_experts;          // experts in the weight tensors; row group g uses expert g % weight_experts
 };
 
 enum GemmMode : int {

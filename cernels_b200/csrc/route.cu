@@ -198,4 +198,15 @@ cudaError_t launch_route(const int32_t* indices, const float* weights, int token
   return cudaGetLastError();
 }
 
+cudaError_t launch_segments(const int* counts, int groups, int* scratch, int* offsets, int* mtile_offsets,
+                            cudaStream_t stream) {
+  cudaError_t err = cudaMemcpyAsync(scratch, counts, static_cast<size_t>(groups) * sizeof(int),
+                                    cudaMemcpyDeviceToDevice, stream);
+  if (err != cudaSuccess) return err;
+  // One "chunk" whose histogram is the given counts.
+  route_scan_kernel<<<1, 1024, static_cast<size_t>(groups) * sizeof(int), stream>>>(scratch, 1, groups, offsets,
+                                                                                    mtile_offsets);
+  return cudaGetLastError();
+}
+
 }  // namespace cernels

@@ -12,8 +12,8 @@ expert slice [r*E/R, (r+1)*E/R) and the contiguous token slice of its batch. One
   4. gather kernel builds the send buffer (local token rows in routed order)
   5. dispatch all_to_all_single (NCCL over NVLink) -> rows for my experts, ordered by
      (source rank, local expert)
-  6. local experts: the experts operator with topk = 1 over the received rows
-     (local expert id per row, weight 1), i.e. the grouped tcgen05 GEMMs + bias
+  6. local experts: the grouped tcgen05 GEMMs read the received rows in place — they are
+     contiguous runs per (source rank, local expert), each run one GEMM group — + bias
   7. combine all_to_all_single back -> every row returns to its source position
   8. combine kernel: out[t] = sum_j w[t, j] * row[inv[t, j]] in fp32, slot order
   (qwen3_next adds its gated shared expert on the local tokens.)
@@ -51,7 +51,8 @@ class Backend:
 
     route(indices int32 [T,k], weights fp32 [T,k], E) -> (offsets [E+1], perm_token, perm_weight, inv)
     gather(x [T,H], perm_token, rows) -> [rows, H]
-    experts(rows [N,H], local_idx int32 [N,1], ones fp32 [N,1]) -> [N,H] (unweighted, + bias)
+    experts(rows [N,H], counts [R * E_local]) -> [N,H]: rows arrive as contiguous runs ordered
+        (source rank, local expert); run g uses local expert g % E_local (unweighted, + bias)
     combine(rows [M,H], inv int32 [T*k], weights fp32 [T,k]) -> [T,H]
     """
 
@@ -64,8 +65,8 @@ class Backend:
 def cuda_backend(layout: int, w1: torch.Tensor, w2: torch.Tensor, b1=None, b2=None) -> Backend:
     from . import ops
 
-    def experts(rows, local_idx, ones):
-        return ops.run_experts(rows, w1, w2, local_idx, ones, 1, layout, False, b1, b2)
+    def experts(rows, counts):
+        return ops.grouped_experts(rows, counts, w1, w2, layout, b1, b2)
 
     return Backend(route=ops.route, gather=ops.gather_rows, experts=experts, combine=ops.combine_rows)
 
@@ -84,8 +85,8 @@ class ExpertParallelMoe:
         self.backend = backend
         self.shared = shared
         self.group = group
-        # route(3) + gather(1) + local experts op(7) + combine(1); + 7 for the shared expert
-        self.launches_per_step = 12 + (7 if shared is not None else 0)
+        # route(3) + gather(1) + grouped experts (segments 1 + 2 GEMMs) + combine(1); + 7 shared
+        self.launches_per_step = 8 + (7 if shared is not None else 0)
 
     # ------------------------------------------------------------ construction
     @classmethod
@@ -149,11 +150,7 @@ class ExpertParallelMoe:
             recv_buf = x.new_empty(n_recv, H)
             dist.all_to_all_single(recv_buf, send_buf, recv_splits, send_splits, group=self.group)
             if n_recv:
-                local_idx = torch.repeat_interleave(
-                    torch.arange(per, device=dev, dtype=torch.int32).repeat(R), recv_counts.reshape(-1),
-                    output_size=n_recv).reshape(n_recv, 1).contiguous()
-                ones = torch.ones(n_recv, 1, dtype=torch.float32, device=dev)
-                rows_out = self.backend.experts(recv_buf, local_idx, ones)
+                rows_out = self.backend.experts(recv_buf, recv_counts.reshape(-1))
             else:
                 rows_out = x.new_empty(0, H)
             back = x.new_empty(n_send, H)

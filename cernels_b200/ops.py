@@ -231,6 +231,33 @@ def route(indices: torch.Tensor, weights: torch.Tensor, experts: int):
     return offsets, perm_token, perm_weight, inv
 
 
+def grouped_experts(rows: torch.Tensor, group_counts: torch.Tensor, gate_up_proj: torch.Tensor,
+                    down_proj: torch.Tensor, layout: int, b1: torch.Tensor | None = None,
+                    b2: torch.Tensor | None = None) -> torch.Tensor:
+    """Expert outputs (+ down bias, unweighted) for rows grouped into contiguous runs:
+    run g has group_counts[g] rows and uses expert g % E of the weights."""
+    _check(rows.is_cuda and rows.dtype == torch.bfloat16 and rows.is_contiguous() and rows.dim() == 2,
+           "rows must be a contiguous [N, H] bf16 CUDA tensor")
+    counts = group_counts.to(device=rows.device, dtype=torch.int32).contiguous()
+    N, H = rows.shape
+    E = gate_up_proj.shape[0]
+    F = gate_up_proj.shape[1] // 2 if layout == _lib.LAYOUT_LINEAR else gate_up_proj.shape[2] // 2
+    G = counts.numel()
+    out = torch.empty_like(rows)
+    if N == 0:
+        return out
+    shape = _lib.MoeShape(int(N), int(H), int(E), int(F), 1, int(layout))
+    ws_shape = _lib.MoeShape(int(N), int(H), int(G), int(F), 1, int(layout))
+    ws_bytes = _lib.workspace_bytes(ws_shape, False)
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=rows.device)
+    with torch.cuda.device(rows.device):
+        rc = _lib.load().cernels_moe_grouped_experts(
+            ctypes.byref(shape), G, counts.data_ptr(), rows.data_ptr(), gate_up_proj.data_ptr(), _ptr(b1),
+            down_proj.data_ptr(), _ptr(b2), out.data_ptr(), ws.data_ptr(), ws_bytes, _stream_handle(rows.device))
+    _lib.check(rc, "cernels_moe_grouped_experts")
+    return out
+
+
 def gather_rows(x: torch.Tensor, perm_token: torch.Tensor, rows: int | None = None) -> torch.Tensor:
     """rows_out[i] = x[perm_token[i]] for i < rows (bf16 [rows, H])."""
     _check(x.is_cuda and x.dtype == torch.bfloat16 and x.is_contiguous() and x.dim() == 2, "x must be [T, H] bf16")

@@ -96,6 +96,20 @@ int cernels_moe_route(const cernels_moe_shape* shape, const int32_t* indices, co
                       int32_t* offsets, int32_t* perm_token, float* perm_weight, int32_t* inv,
                       void* workspace, size_t workspace_bytes, void* stream);
 
+/* Expert compute on rows already grouped into `groups` contiguous runs: run g holds
+ * group_counts[g] rows (device int32 array) and uses expert g % shape->experts of the
+ * weights (groups must be a multiple of shape->experts). Writes each row's unweighted expert
+ * output (+ down_bias) to rows_out in the same order. shape->tokens is the row capacity of
+ * rows_in / rows_out; shape->topk is ignored. Workspace: cernels_moe_workspace_bytes() of the
+ * shape with experts = groups and topk = 1. This is the receive side of expert parallelism:
+ * rows arrive from the dispatch all-to-all ordered by (source rank, local expert), so the
+ * grouped GEMMs read them in place. Replaces, per expert, the two cublasGemmEx calls + bias +
+ * SwiGLU of src/kops/gpt_oss_moe_experts/csrc/gpt_oss_moe_experts.cu:200-242. */
+int cernels_moe_grouped_experts(const cernels_moe_shape* shape, int32_t groups, const int32_t* group_counts,
+                                const void* rows_in, const void* gate_up_proj, const float* gate_up_bias,
+                                const void* down_proj, const float* down_bias, void* rows_out, void* workspace,
+                                size_t workspace_bytes, void* stream);
+
 /* Gather: rows_out[i, :] = x[perm_token[i], :] for i < rows ([rows, H] bf16). Replaces
  * gather_kernel (src/kops/cohere2_moe_experts/csrc/cohere2_moe_experts.cu:58-65). Used by
  * expert parallelism to build the dispatch send buffer in routed order. */

@@ -268,3 +268,37 @@ def test_decode_streaming_shapes(T, H, E, F, k):
     assert_close(out, oracle_out(x, w1, w2, idx, w, LAYOUT_LINEAR))
     none = run_op(x, w1, w2, torch.full_like(idx, -1), w, k, LAYOUT_LINEAR, True)
     assert torch.count_nonzero(none) == 0
+
+
+@pytest.mark.parametrize("layout", [LAYOUT_LINEAR, LAYOUT_GPTOSS])
+def test_grouped_experts_segments(layout):
+    """cernels_moe_grouped_experts: rows in runs ordered (source rank, local expert)."""
+    g = torch.Generator().manual_seed(5)
+    R, E, H, F = 4, 3, 256, 136
+    counts = torch.randint(0, 200, (R * E,), generator=g)
+    counts[1] = 0
+    counts[5] = 300  # several m-tiles in one run
+    N = int(counts.sum())
+    rows = torch.randn(N, H, generator=g).to(torch.bfloat16)
+    if layout == LAYOUT_LINEAR:
+        w1 = (torch.randn(E, 2 * F, H, generator=g) * 0.05).to(torch.bfloat16)
+        w2 = (torch.randn(E, H, F, generator=g) * 0.05).to(torch.bfloat16)
+        b1 = b2 = None
+    else:
+        w1 = (torch.randn(E, H, 2 * F, generator=g) * 0.05).to(torch.bfloat16)
+        w2 = (torch.randn(E, F, H, generator=g) * 0.05).to(torch.bfloat16)
+        b1 = torch.randn(E, 2 * F, generator=g) * 0.1
+        b2 = torch.randn(E, H, generator=g) * 0.1
+    out = ops.grouped_experts(rows.to(DEV), counts.to(DEV), w1.to(DEV), w2.to(DEV), layout,
+                              None if b1 is None else b1.to(DEV), None if b2 is None else b2.to(DEV))
+    ref = np.zeros((N, H), np.float32)
+    start = 0
+    for gi, c in enumerate(counts.tolist()):
+        e = gi % E
+        if c:
+            ref[start:start + c] = O.expert_rows(rows[start:start + c].float().numpy(), w1[e].float().numpy(),
+                                                 w2[e].float().numpy(), layout,
+                                                 None if b1 is None else b1[e].numpy(),
+                                                 None if b2 is None else b2[e].numpy())
+        start += c
+    assert_close(out, ref)
