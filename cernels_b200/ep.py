@@ -11,7 +11,9 @@ expert slice [r*E/R, (r+1)*E/R) and the contiguous token slice of its batch. One
      device->host copy gives the split sizes NCCL needs
   4. gather kernel builds the send buffer (local token rows in routed order)
   5. dispatch all_to_all_single (NCCL over NVLink) -> rows for my experts, ordered by
-     (source rank, local expert)
+     (source rank, local expert). Each destination segment is cut into C contiguous row
+     pieces and the send buffer is laid out chunk-major, so chunk c's dispatch, chunk c-1's
+     expert GEMMs and chunk c-2's return overlap (NCCL runs on its own stream)
   6. local experts: the grouped tcgen05 GEMMs read the received rows in place — they are
      contiguous runs per (source rank, local expert), each run one GEMM group — + bias
   7. combine all_to_all_single back -> every row returns to its source position
@@ -27,6 +29,7 @@ from __future__ import annotations
 import dataclasses
 from typing import Callable
 
+import numpy as np
 import torch
 import torch.distributed as dist
 
@@ -75,7 +78,7 @@ class ExpertParallelMoe:
     """EP forward over a process group; weights of the local expert slice only."""
 
     def __init__(self, experts: int, topk: int, rank: int, world: int, router: Callable, backend: Backend,
-                 shared: Callable | None = None, group=None):
+                 shared: Callable | None = None, group=None, chunks: int | None = None):
         self.E = experts
         self.k = topk
         self.rank = rank
@@ -85,8 +88,9 @@ class ExpertParallelMoe:
         self.backend = backend
         self.shared = shared
         self.group = group
-        # route(3) + gather(1) + grouped experts (segments 1 + 2 GEMMs) + combine(1); + 7 shared
-        self.launches_per_step = 8 + (7 if shared is not None else 0)
+        self.chunks = chunks  # None: chosen from the row count
+        # route(3) + gather(1) + combine(1) + per chunk grouped experts (scan + 2 GEMMs); + 7 shared
+        self.launches_per_step = 5 + 3 * 4 + (7 if shared is not None else 0)
 
     # ------------------------------------------------------------ construction
     @classmethod
@@ -126,6 +130,23 @@ class ExpertParallelMoe:
         raise ValueError(f"expert parallelism is not used for {kind}")
 
     # ------------------------------------------------------------ forward
+    @staticmethod
+    def piece_counts(counts: np.ndarray, chunks: int) -> np.ndarray:
+        """Splits one destination segment (rows of consecutive experts with `counts` rows each)
+        into `chunks` contiguous row pieces; returns [chunks, len(counts)] rows per expert per piece."""
+        n = int(counts.sum())
+        bounds = (np.arange(chunks + 1, dtype=np.int64) * n) // chunks
+        starts = np.concatenate([[0], np.cumsum(counts)[:-1]])
+        ends = starts + counts
+        lo = np.maximum(starts[None, :], bounds[:-1, None])
+        hi = np.minimum(ends[None, :], bounds[1:, None])
+        return np.maximum(hi - lo, 0)
+
+    def chunks_for(self, rows: int) -> int:
+        if self.chunks is not None:
+            return self.chunks
+        return 4 if rows >= 8192 else (2 if rows >= 2048 else 1)
+
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         R, E, k = self.world, self.E, self.k
         per = E // R
@@ -134,28 +155,59 @@ class ExpertParallelMoe:
             idx, w = self.router(x)
             idx = idx.to(torch.int32).contiguous()
             w = w.float().contiguous()
-            T = x.shape[0]
+            H = x.shape[1]
             offsets, perm_token, _perm_weight, inv = self.backend.route(idx, w, E)
             # per-expert counts, grouped by destination rank -> [R, per]
             send_counts = (offsets[1:] - offsets[:-1]).to(torch.int64).reshape(R, per)
             recv_counts = torch.empty_like(send_counts)
             dist.all_to_all_single(recv_counts, send_counts, group=self.group)
-            counts_host = torch.stack([send_counts.sum(1), recv_counts.sum(1)]).cpu()  # one small D2H
-            send_splits = counts_host[0].tolist()
-            recv_splits = counts_host[1].tolist()
-            n_send = int(sum(send_splits))
-            n_recv = int(sum(recv_splits))
-            H = x.shape[1]
-            send_buf = self.backend.gather(x, perm_token, n_send) if n_send else x.new_empty(0, H)
-            recv_buf = x.new_empty(n_recv, H)
-            dist.all_to_all_single(recv_buf, send_buf, recv_splits, send_splits, group=self.group)
-            if n_recv:
-                rows_out = self.backend.experts(recv_buf, recv_counts.reshape(-1))
-            else:
-                rows_out = x.new_empty(0, H)
+            host = torch.stack([send_counts, recv_counts]).cpu().numpy()  # the one device->host copy
+            sc, rc = host[0], host[1]
+            n_send = int(sc.sum())
+            C = self.chunks_for(n_send)
+            # send pieces [C, R, per] and receive pieces [C, R(src), per]
+            send_p = np.stack([self.piece_counts(sc[d], C) for d in range(R)], axis=1)
+            recv_p = np.stack([self.piece_counts(rc[s_], C) for s_ in range(R)], axis=1)
+            # chunk-major order of the routed rows: for c: for d: piece (c, d)
+            seg_start = np.concatenate([[0], np.cumsum(sc.sum(1))[:-1]])
+            piece_start = np.zeros((C, R), dtype=np.int64)
+            for d in range(R):
+                piece_start[:, d] = seg_start[d] + np.concatenate([[0], np.cumsum(send_p[:, d].sum(1))[:-1]])
+            order = np.concatenate([np.arange(piece_start[c, d], piece_start[c, d] + send_p[c, d].sum())
+                                    for c in range(C) for d in range(R)]) if n_send else np.zeros(0, np.int64)
+            order_t = torch.from_numpy(order).to(dev, non_blocking=True)
+            pos = torch.empty(max(n_send, 1), dtype=torch.int64, device=dev)
+            pos[order_t] = torch.arange(n_send, device=dev)
+            inv2 = torch.where(inv >= 0, pos[inv.clamp(min=0).long()], -1).to(torch.int32).contiguous()
+            send_buf = (self.backend.gather(x, perm_token[order_t].contiguous(), n_send) if n_send
+                        else x.new_empty(0, H))
+            # pipeline: dispatch all chunks, then per chunk: wait, experts, return
+            send_rows = send_p.sum(2)   # [C, R]
+            recv_rows = recv_p.sum(2)   # [C, R]
+            recv_bufs, handles, s_off = [], [], 0
+            for c in range(C):
+                ns, nr = int(send_rows[c].sum()), int(recv_rows[c].sum())
+                rb = x.new_empty(nr, H)
+                handles.append(dist.all_to_all_single(rb, send_buf[s_off:s_off + ns], recv_rows[c].tolist(),
+                                                      send_rows[c].tolist(), group=self.group, async_op=True))
+                recv_bufs.append(rb)
+                s_off += ns
             back = x.new_empty(n_send, H)
-            dist.all_to_all_single(back, rows_out, send_splits, recv_splits, group=self.group)
-            out = self.backend.combine(back, inv, w)
+            ret_handles, s_off = [], 0
+            for c in range(C):
+                ns, nr = int(send_rows[c].sum()), int(recv_rows[c].sum())
+                handles[c].wait()
+                if nr:
+                    counts_c = torch.from_numpy(recv_p[c].reshape(-1).astype(np.int32)).to(dev, non_blocking=True)
+                    rows_out = self.backend.experts(recv_bufs[c], counts_c)
+                else:
+                    rows_out = x.new_empty(0, H)
+                ret_handles.append(dist.all_to_all_single(back[s_off:s_off + ns], rows_out, send_rows[c].tolist(),
+                                                          recv_rows[c].tolist(), group=self.group, async_op=True))
+                s_off += ns
+            for h in ret_handles:
+                h.wait()
+            out = self.backend.combine(back, inv2, w)
             if self.shared is not None:
                 out = out + self.shared(x)
             return out

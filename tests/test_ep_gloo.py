@@ -93,7 +93,7 @@ def cpu_backend(p, e0, e1):
     return ep.Backend(route=route, gather=gather, experts=experts, combine=combine)
 
 
-def _worker(rank, world, port, layout, result_q):
+def _worker(rank, world, port, layout, result_q, chunks=None):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     dist.init_process_group("gloo", rank=rank, world_size=world)
@@ -101,7 +101,7 @@ def _worker(rank, world, port, layout, result_q):
         p = make_problem(layout)
         E = p["w1"].shape[0]
         e0, e1 = ep.expert_shard(E, rank, world)
-        moe = ep.ExpertParallelMoe(E, p["k"], rank, world, router_fn(p), cpu_backend(p, e0, e1))
+        moe = ep.ExpertParallelMoe(E, p["k"], rank, world, router_fn(p), cpu_backend(p, e0, e1), chunks=chunks)
         shard = ep.token_shard(p["x"].shape[0], rank, world)
         out = moe.forward(p["x"][shard].contiguous())
         result_q.put((rank, out.float().numpy()))
@@ -109,13 +109,13 @@ def _worker(rank, world, port, layout, result_q):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("world", [2, 4])
+@pytest.mark.parametrize("world,chunks", [(2, None), (2, 3), (4, 2)])
 @pytest.mark.parametrize("layout", [O.LAYOUT_LINEAR, O.LAYOUT_GPTOSS])
-def test_ep_matches_single_process_oracle(world, layout):
+def test_ep_matches_single_process_oracle(world, chunks, layout):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, layout, q)) for r in range(world)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, layout, q, chunks)) for r in range(world)]
     for pr in procs:
         pr.start()
     results = dict(q.get(timeout=120) for _ in range(world))
@@ -129,6 +129,18 @@ def test_ep_matches_single_process_oracle(world, layout):
                         w.numpy(), layout, None if p["b1"] is None else p["b1"].numpy(),
                         None if p["b2"] is None else p["b2"].numpy())
     assert O.rel_err(out, ref) <= 1e-2
+
+
+def test_piece_counts_partition_each_segment():
+    rng = np.random.default_rng(0)
+    for _ in range(50):
+        counts = rng.integers(0, 40, size=rng.integers(1, 9))
+        for C in (1, 2, 3, 5):
+            p = ep.ExpertParallelMoe.piece_counts(counts, C)
+            assert p.shape == (C, counts.size)
+            assert np.array_equal(p.sum(0), counts)
+            sizes = p.sum(1)
+            assert sizes.max() - sizes.min() <= 1
 
 
 def test_shards_cover_tokens_and_experts():
