@@ -143,9 +143,9 @@ class ExpertParallelMoe:
         return np.maximum(hi - lo, 0)
 
     def chunks_for(self, rows: int) -> int:
-        if self.chunks is not None:
-            return self.chunks
-        return 4 if rows >= 8192 else (2 if rows >= 2048 else 1)
+        # One chunk by default: on B200 the host-side chunk bookkeeping and the smaller GEMM
+        # calls cost more than the overlap gains at 2 ranks (measured); callers can opt in.
+        return 1 if self.chunks is None else max(1, int(self.chunks))
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         R, E, k = self.world, self.E, self.k
@@ -168,19 +168,23 @@ class ExpertParallelMoe:
             # send pieces [C, R, per] and receive pieces [C, R(src), per]
             send_p = np.stack([self.piece_counts(sc[d], C) for d in range(R)], axis=1)
             recv_p = np.stack([self.piece_counts(rc[s_], C) for s_ in range(R)], axis=1)
-            # chunk-major order of the routed rows: for c: for d: piece (c, d)
-            seg_start = np.concatenate([[0], np.cumsum(sc.sum(1))[:-1]])
-            piece_start = np.zeros((C, R), dtype=np.int64)
-            for d in range(R):
-                piece_start[:, d] = seg_start[d] + np.concatenate([[0], np.cumsum(send_p[:, d].sum(1))[:-1]])
-            order = np.concatenate([np.arange(piece_start[c, d], piece_start[c, d] + send_p[c, d].sum())
-                                    for c in range(C) for d in range(R)]) if n_send else np.zeros(0, np.int64)
-            order_t = torch.from_numpy(order).to(dev, non_blocking=True)
-            pos = torch.empty(max(n_send, 1), dtype=torch.int64, device=dev)
-            pos[order_t] = torch.arange(n_send, device=dev)
-            inv2 = torch.where(inv >= 0, pos[inv.clamp(min=0).long()], -1).to(torch.int32).contiguous()
-            send_buf = (self.backend.gather(x, perm_token[order_t].contiguous(), n_send) if n_send
-                        else x.new_empty(0, H))
+            if C == 1:
+                inv2 = inv
+                send_buf = self.backend.gather(x, perm_token, n_send) if n_send else x.new_empty(0, H)
+            else:
+                # chunk-major order of the routed rows: for c: for d: piece (c, d)
+                seg_start = np.concatenate([[0], np.cumsum(sc.sum(1))[:-1]])
+                piece_start = np.zeros((C, R), dtype=np.int64)
+                for d in range(R):
+                    piece_start[:, d] = seg_start[d] + np.concatenate([[0], np.cumsum(send_p[:, d].sum(1))[:-1]])
+                order = np.concatenate([np.arange(piece_start[c, d], piece_start[c, d] + send_p[c, d].sum())
+                                        for c in range(C) for d in range(R)]) if n_send else np.zeros(0, np.int64)
+                order_t = torch.from_numpy(order).to(dev)
+                pos = torch.empty(max(n_send, 1), dtype=torch.int64, device=dev)
+                pos[order_t] = torch.arange(n_send, device=dev)
+                inv2 = torch.where(inv >= 0, pos[inv.clamp(min=0).long()], -1).to(torch.int32).contiguous()
+                send_buf = (self.backend.gather(x, perm_token[order_t].contiguous(), n_send) if n_send
+                            else x.new_empty(0, H))
             # pipeline: dispatch all chunks, then per chunk: wait, experts, return
             send_rows = send_p.sum(2)   # [C, R]
             recv_rows = recv_p.sum(2)   # [C, R]
