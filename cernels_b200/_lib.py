@@ -48,6 +48,7 @@ PROTOTYPES = {
                                                      ctypes.POINTER(ctypes.c_float)]),
     "cernels_moe_experts_decode_noalloc": (ctypes.c_int, [_SHAPE_P, _VP, _VP, _VP, _VP, _VP, _VP, _VP, _VP, _VP]),
     "cernels_moe_grouped_experts": (ctypes.c_int, [_SHAPE_P, _I32, _VP, _VP, _VP, _VP, _VP, _VP, _VP, _VP, _SZ, _VP]),
+    "cernels_router_topk": (ctypes.c_int, [_VP, _I32, _I32, _I32, _I32, _I32, _I32, _VP, _VP, _VP]),
     "cernels_moe_route": (ctypes.c_int, [_SHAPE_P, _VP, _VP, _VP, _VP, _VP, _VP, _VP, _SZ, _VP]),
     "cernels_moe_gather": (ctypes.c_int, [_VP, _VP, _I32, _I32, _VP, _VP]),
     "cernels_moe_combine": (ctypes.c_int, [_VP, _VP, _VP, _I32, _I32, _I32, _VP, _VP]),

@@ -345,6 +345,17 @@ int cernels_moe_grouped_experts(const cernels_moe_shape* shape, int32_t groups, 
   return cuda_rc(launch_grouped_gemm(gptoss ? kDownGptOss : kDownLinear, g2, sms, stream));
 }
 
+int cernels_router_topk(const void* logits, int32_t logits_bf16, int32_t tokens, int32_t experts, int32_t topk,
+                        int32_t mode, int32_t renorm, int32_t* indices, float* weights, void* stream) {
+  if (tokens < 0 || experts <= 0 || experts > 1024 || topk <= 0 || topk > 32 || topk > experts)
+    return CERNELS_E_INVALID_SHAPE;
+  if (mode != CERNELS_ROUTER_TOPK_SOFTMAX && mode != CERNELS_ROUTER_SOFTMAX_TOPK) return CERNELS_E_INVALID_SHAPE;
+  if (tokens == 0) return CERNELS_OK;
+  if (!logits || !indices || !weights) return CERNELS_E_NULL;
+  return cuda_rc(launch_router_topk(logits, logits_bf16 != 0, tokens, experts, topk, mode, renorm != 0, indices,
+                                    weights, static_cast<cudaStream_t>(stream)));
+}
+
 int cernels_moe_route(const cernels_moe_shape* shape, const int32_t* indices, const float* weights,
                       int32_t* offsets, int32_t* perm_token, float* perm_weight, int32_t* inv, void* workspace,
                       size_t workspace_bytes, void* stream_ptr) {

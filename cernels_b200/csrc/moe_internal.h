@@ -103,6 +103,11 @@ struct DecodeArgs {
 };
 cudaError_t launch_decode(const DecodeArgs& a, const DecodeWorkspace& ws, cudaStream_t stream);
 
+// Router tail (router.cu). mode 0: top-k of the logits, softmax over the k values rounded to
+// bf16; mode 1: softmax over all experts (fp32), top-k, optional renormalisation.
+cudaError_t launch_router_topk(const void* logits, int bf16, int tokens, int experts, int topk, int mode, int renorm,
+                               int32_t* idx, float* w, cudaStream_t stream);
+
 int device_sm_count();
 
 }  // namespace cernels

@@ -4,7 +4,7 @@ The reference is single-GPU; expert parallelism is the north star's multi-GPU sc
 the large-token configurations (qwen3_next, gpt_oss). Rank r of R owns the contiguous
 expert slice [r*E/R, (r+1)*E/R) and the contiguous token slice of its batch. One forward:
 
-  1. router on the local tokens (torch, as in the reference loaders)
+  1. router on the local tokens (linear in cuBLAS, top-k/softmax in one kernel)
   2. routing kernel over the GLOBAL expert ids: offsets, stable permutation, inverse map
      — rows bound for rank d are contiguous because experts are sharded contiguously
   3. per-expert counts for each destination exchanged with all_to_all_single; one small
@@ -107,9 +107,10 @@ class ExpertParallelMoe:
             b2 = ex.down_proj_bias.data[e0:e1].float().contiguous()
             backend = cuda_backend(LAYOUT_GPTOSS, w1, w2, b1, b2)
 
+            from .registry import gpt_oss_moe_experts as go
+
             def router(x):
-                _, scores, idx = module.router(x)
-                return idx, scores
+                return go.route(x, module)
 
             return cls(E, int(module.router.top_k), rank, world, router, backend, None, group)
         if kind == "qwen3_next":
@@ -122,8 +123,7 @@ class ExpertParallelMoe:
                                    ex.down_proj.data[e0:e1].contiguous())
 
             def router(x):
-                _, scores, idx = module.gate(x)
-                return idx, scores
+                return qn.route(x, module)
 
             return cls(E, int(module.gate.top_k), rank, world, router, backend, lambda x: qn.shared_expert(x, module),
                        group)
@@ -142,7 +142,7 @@ class ExpertParallelMoe:
         hi = np.minimum(ends[None, :], bounds[1:, None])
         return np.maximum(hi - lo, 0)
 
-    def chunks_for(self, rows: int) -> int:
+    def chunks_for(self, rows: int = 0) -> int:
         # One chunk by default: on B200 the host-side chunk bookkeeping and the smaller GEMM
         # calls cost more than the overlap gains at 2 ranks (measured); callers can opt in.
         return 1 if self.chunks is None else max(1, int(self.chunks))
@@ -161,17 +161,24 @@ class ExpertParallelMoe:
             send_counts = (offsets[1:] - offsets[:-1]).to(torch.int64).reshape(R, per)
             recv_counts = torch.empty_like(send_counts)
             dist.all_to_all_single(recv_counts, send_counts, group=self.group)
+            C = self.chunks_for(0)
+            if C == 1:
+                # Enqueue the gather before the host copy below so it runs while the host waits;
+                # rows past the valid count gather token 0 (route zero-fills) and are not sent.
+                tk = idx.numel()
+                send_all = self.backend.gather(x, perm_token, tk) if tk else x.new_empty(0, H)
             host = torch.stack([send_counts, recv_counts]).cpu().numpy()  # the one device->host copy
             sc, rc = host[0], host[1]
             n_send = int(sc.sum())
-            C = self.chunks_for(n_send)
-            # send pieces [C, R, per] and receive pieces [C, R(src), per]
-            send_p = np.stack([self.piece_counts(sc[d], C) for d in range(R)], axis=1)
-            recv_p = np.stack([self.piece_counts(rc[s_], C) for s_ in range(R)], axis=1)
             if C == 1:
                 inv2 = inv
-                send_buf = self.backend.gather(x, perm_token, n_send) if n_send else x.new_empty(0, H)
+                send_buf = send_all[:n_send]
+                send_rows = sc.sum(1)[None, :]
+                recv_rows = rc.sum(1)[None, :]
+                recv_p = None
             else:
+                send_p = np.stack([self.piece_counts(sc[d], C) for d in range(R)], axis=1)
+                recv_p = np.stack([self.piece_counts(rc[s_], C) for s_ in range(R)], axis=1)
                 # chunk-major order of the routed rows: for c: for d: piece (c, d)
                 seg_start = np.concatenate([[0], np.cumsum(sc.sum(1))[:-1]])
                 piece_start = np.zeros((C, R), dtype=np.int64)
@@ -185,9 +192,9 @@ class ExpertParallelMoe:
                 inv2 = torch.where(inv >= 0, pos[inv.clamp(min=0).long()], -1).to(torch.int32).contiguous()
                 send_buf = (self.backend.gather(x, perm_token[order_t].contiguous(), n_send) if n_send
                             else x.new_empty(0, H))
+                send_rows = send_p.sum(2)   # [C, R]
+                recv_rows = recv_p.sum(2)   # [C, R]
             # pipeline: dispatch all chunks, then per chunk: wait, experts, return
-            send_rows = send_p.sum(2)   # [C, R]
-            recv_rows = recv_p.sum(2)   # [C, R]
             recv_bufs, handles, s_off = [], [], 0
             for c in range(C):
                 ns, nr = int(send_rows[c].sum()), int(recv_rows[c].sum())
@@ -202,7 +209,8 @@ class ExpertParallelMoe:
                 ns, nr = int(send_rows[c].sum()), int(recv_rows[c].sum())
                 handles[c].wait()
                 if nr:
-                    counts_c = torch.from_numpy(recv_p[c].reshape(-1).astype(np.int32)).to(dev, non_blocking=True)
+                    counts_c = (recv_counts.reshape(-1) if recv_p is None else
+                                torch.from_numpy(recv_p[c].reshape(-1).astype(np.int32)).to(dev))
                     rows_out = self.backend.experts(recv_bufs[c], counts_c)
                 else:
                     rows_out = x.new_empty(0, H)

@@ -258,6 +258,27 @@ def grouped_experts(rows: torch.Tensor, group_counts: torch.Tensor, gate_up_proj
     return out
 
 
+ROUTER_TOPK_SOFTMAX = 0
+ROUTER_SOFTMAX_TOPK = 1
+
+
+def router_topk(logits: torch.Tensor, topk: int, mode: int, renorm: bool = False):
+    """Top-k expert ids (int32) and fp32 routing weights from router logits [T, E] in one launch
+    (see cernels_router_topk in include/cernels_b200.h)."""
+    _check(logits.is_cuda and logits.dim() == 2 and logits.dtype in (torch.bfloat16, torch.float32),
+           "logits must be a [T, E] bf16 or fp32 CUDA tensor")
+    logits = logits.contiguous()
+    T, E = logits.shape
+    idx = torch.empty(T, topk, dtype=torch.int32, device=logits.device)
+    w = torch.empty(T, topk, dtype=torch.float32, device=logits.device)
+    with torch.cuda.device(logits.device):
+        rc = _lib.load().cernels_router_topk(logits.data_ptr(), int(logits.dtype == torch.bfloat16), T, E, int(topk),
+                                             int(mode), int(bool(renorm)), idx.data_ptr(), w.data_ptr(),
+                                             _stream_handle(logits.device))
+    _lib.check(rc, "cernels_router_topk")
+    return idx, w
+
+
 def gather_rows(x: torch.Tensor, perm_token: torch.Tensor, rows: int | None = None) -> torch.Tensor:
     """rows_out[i] = x[perm_token[i]] for i < rows (bf16 [rows, H])."""
     _check(x.is_cuda and x.dtype == torch.bfloat16 and x.is_contiguous() and x.dim() == 2, "x must be [T, H] bf16")

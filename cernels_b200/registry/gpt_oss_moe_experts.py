@@ -1,8 +1,8 @@
 """gpt_oss_moe_experts loader — drop-in for src/kops/registry/gpt_oss_moe_experts.py.
 
-``kernel(x, mlp)`` takes hidden states [B, S, H] and a GptOssMLP. The router (linear +
-bias, top-k, softmax over the k logits) runs in torch in the timed path, as in the
-reference loader; the CUDA op does routing, both grouped GEMMs (with biases) and the
+``kernel(x, mlp)`` takes hidden states [B, S, H] and a GptOssMLP. The router runs in the
+timed path, as in the reference loader: its linear in cuBLAS (torch), its top-k + softmax in
+one kernel (cernels_router_topk); the CUDA op does routing, both grouped GEMMs (with biases) and the
 clamped interleaved SwiGLU. Weights are consumed in place in the transformers layout
 ([E, H, 2F] interleaved gate/up, [E, F, H]); only the fp32 bias casts are cached on the
 module, as the reference does (its ``_kops_weights``).
@@ -11,7 +11,7 @@ module, as the reference does (its ``_kops_weights``).
 import torch
 
 from .. import ops
-from ._common import module_cache, routing_tensors
+from ._common import module_cache
 
 
 def _weights(experts):
@@ -22,15 +22,21 @@ def _weights(experts):
     return experts.gate_up_proj.data.contiguous(), b1, experts.down_proj.data.contiguous(), b2
 
 
+def route(xf, mlp):
+    """transformers GptOssTopKRouter: logits = x W^T + b (cuBLAS via torch), then top-k and the
+    softmax over the k logits in one kernel (int32 ids, fp32 weights)."""
+    logits = torch.nn.functional.linear(xf, mlp.router.weight, mlp.router.bias)
+    return ops.router_topk(logits, int(mlp.router.top_k), ops.ROUTER_TOPK_SOFTMAX)
+
+
 def kernel(x, mlp):
     if mlp is None:
         raise RuntimeError("mlp module not available (meta device)")
     bsz, seqlen, hidden = x.shape
     xf = x.reshape(-1, hidden).contiguous()
     with torch.no_grad():
-        _logits, scores, indices = mlp.router(xf)
+        idx, w = route(xf, mlp)
         w1, b1, w2, b2 = _weights(mlp.experts)
-        idx, w = routing_tensors(indices, scores)
         out = ops.gpt_oss_moe_experts(xf, w1, b1, w2, b2, idx, w, int(mlp.router.top_k))
     return out.reshape(bsz, seqlen, hidden)
 
@@ -41,8 +47,7 @@ def decode_kernel(x, mlp):
     bsz, seqlen, hidden = x.shape
     xf = x.reshape(-1, hidden).contiguous()
     with torch.no_grad():
-        _logits, scores, indices = mlp.router(xf)
+        idx, w = route(xf, mlp)
         w1, b1, w2, b2 = _weights(mlp.experts)
-        idx, w = routing_tensors(indices, scores)
         out = ops.gpt_oss_moe_experts_decode(xf, w1, b1, w2, b2, idx, w, int(mlp.router.top_k))
     return out.reshape(bsz, seqlen, hidden)

@@ -1,8 +1,8 @@
 """qwen3_next_moe_experts loader — drop-in for src/kops/registry/qwen3_next_moe_experts.py.
 
 ``kernel(x, block)`` takes the raw hidden states [B, S, H] and a
-Qwen3NextSparseMoeBlock. As in the reference loader, the router (block.gate: linear +
-fp32 softmax + top-k + renorm) runs in torch in the timed path; the routed experts run in
+Qwen3NextSparseMoeBlock. As in the reference loader, the router runs in the timed path:
+its linear in cuBLAS (torch), softmax + top-k + renorm in one kernel (cernels_router_topk); the routed experts run in
 the CUDA op; the always-on shared expert ``sigmoid(shared_expert_gate(x)) *
 shared_expert(x)`` runs through the same CUDA grouped-GEMM path as a one-expert,
 one-slot problem whose router weight is the sigmoid gate (its gate/up weights are
@@ -12,7 +12,7 @@ concatenated once into the [1, 2Fs, H] layout and cached on the block).
 import torch
 
 from .. import ops
-from ._common import module_cache, routing_tensors
+from ._common import module_cache
 
 
 def _shared_weights(block):
@@ -38,15 +38,21 @@ def shared_expert(xf: torch.Tensor, block) -> torch.Tensor:
     return ops.qwen3_next_moe_experts(xf, w1, w2, idx, gate, 1)
 
 
+def route(xf, block):
+    """transformers Qwen3NextTopKRouter: logits = x W^T (cuBLAS via torch), then fp32 softmax,
+    top-k and renormalisation in one kernel (int32 ids, fp32 weights)."""
+    logits = torch.nn.functional.linear(xf, block.gate.weight)
+    return ops.router_topk(logits, int(block.gate.top_k), ops.ROUTER_SOFTMAX_TOPK, bool(block.gate.norm_topk_prob))
+
+
 def kernel(x, block):
     if block is None:
         raise RuntimeError("block module not available (meta device)")
     bsz, seqlen, hidden = x.shape
     xf = x.reshape(-1, hidden).contiguous()
     with torch.no_grad():
-        _logits, scores, indices = block.gate(xf)
+        idx, w = route(xf, block)
         e = block.experts
-        idx, w = routing_tensors(indices, scores)
         routed = ops.qwen3_next_moe_experts(xf, e.gate_up_proj.data.contiguous(), e.down_proj.data.contiguous(),
                                             idx, w, int(block.gate.top_k))
         out = routed + shared_expert(xf, block)
@@ -60,9 +66,8 @@ def decode_kernel(x, block):
     bsz, seqlen, hidden = x.shape
     xf = x.reshape(-1, hidden).contiguous()
     with torch.no_grad():
-        _logits, scores, indices = block.gate(xf)
+        idx, w = route(xf, block)
         e = block.experts
-        idx, w = routing_tensors(indices, scores)
         routed = ops.qwen3_next_moe_experts_decode(xf, e.gate_up_proj.data.contiguous(),
                                                    e.down_proj.data.contiguous(), idx, w, int(block.gate.top_k))
         out = routed + shared_expert(xf, block)

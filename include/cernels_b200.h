@@ -110,6 +110,20 @@ int cernels_moe_grouped_experts(const cernels_moe_shape* shape, int32_t groups, 
                                 const void* down_proj, const float* down_bias, void* rows_out, void* workspace,
                                 size_t workspace_bytes, void* stream);
 
+/* Router tail: from router logits [T, E] (bf16 if logits_bf16, else fp32) to top-k expert ids
+ * (int32 [T, topk], descending, ties to the lower id) and routing weights (fp32 [T, topk]).
+ * mode CERNELS_ROUTER_TOPK_SOFTMAX: softmax over the k selected logits, rounded to bf16 — the
+ *   transformers gpt-oss router (models/gpt_oss/modeling_gpt_oss.py:117-131);
+ * mode CERNELS_ROUTER_SOFTMAX_TOPK: softmax over all E in fp32, top-k, renormalised to sum 1
+ *   when renorm — the transformers qwen3-next router (models/qwen3_next/modeling_qwen3_next.py:761-780).
+ * Replaces the torch topk / softmax / casts the reference loaders run
+ * (src/kops/registry/gpt_oss_moe_experts.py:35-45, src/kops/registry/qwen3_next_moe_experts.py:28-37).
+ * E <= 1024, topk <= 32. */
+#define CERNELS_ROUTER_TOPK_SOFTMAX 0
+#define CERNELS_ROUTER_SOFTMAX_TOPK 1
+int cernels_router_topk(const void* logits, int32_t logits_bf16, int32_t tokens, int32_t experts, int32_t topk,
+                        int32_t mode, int32_t renorm, int32_t* indices, float* weights, void* stream);
+
 /* Gather: rows_out[i, :] = x[perm_token[i], :] for i < rows ([rows, H] bf16). Replaces
  * gather_kernel (src/kops/cohere2_moe_experts/csrc/cohere2_moe_experts.cu:58-65). Used by
  * expert parallelism to build the dispatch send buffer in routed order. */

@@ -58,12 +58,13 @@ def cpu_backend(p, e0, e1):
     def route(idx, w, E):
         offsets, order, inv = O.route(idx.numpy(), E)
         k = idx.shape[1]
-        perm_token = torch.from_numpy((order // k).astype(np.int32))
+        perm_token = torch.zeros(idx.numel(), dtype=torch.int32)
+        perm_token[:order.size] = torch.from_numpy((order // k).astype(np.int32))
         perm_w = w.reshape(-1)[torch.from_numpy(order)]
         return torch.from_numpy(offsets), perm_token, perm_w, torch.from_numpy(inv)
 
     def gather(x, perm_token, rows):
-        return x[perm_token[:rows].long()].contiguous()
+        return x[perm_token[:rows].long().clamp(0, x.shape[0] - 1)].contiguous()
 
     def experts(rows, counts):
         out = np.zeros((rows.shape[0], rows.shape[1]), np.float32)

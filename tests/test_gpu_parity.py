@@ -302,3 +302,45 @@ def test_grouped_experts_segments(layout):
                                                  None if b2 is None else b2[e].numpy())
         start += c
     assert_close(out, ref)
+
+
+@pytest.mark.parametrize("mode,E,k,renorm", [(0, 32, 4, False), (1, 512, 10, True), (1, 128, 8, False),
+                                             (0, 64, 6, False), (1, 1000, 32, True)])
+def test_router_topk_matches_torch(mode, E, k, renorm):
+    g = torch.Generator().manual_seed(E + k)
+    T = 777
+    logits32 = torch.randn(T, E, generator=g).to(DEV)
+    idx, w = ops.router_topk(logits32, k, mode, renorm)
+    if mode == 0:
+        v, i = torch.topk(logits32, k, dim=-1)
+        ref_w = torch.softmax(v, dim=-1).to(torch.bfloat16).float()
+    else:
+        p = torch.softmax(logits32, dim=-1)
+        v, i = torch.topk(p, k, dim=-1)
+        ref_w = v / v.sum(-1, keepdim=True) if renorm else v
+    assert torch.equal(idx.long(), i)  # fp32 random logits: no ties
+    assert torch.allclose(w, ref_w, atol=1e-5, rtol=1e-2)
+    # bf16 logits: the selected values equal torch's sorted top-k (ties may permute ids)
+    lb = logits32.to(torch.bfloat16)
+    idx_b, _ = ops.router_topk(lb, k, mode, renorm)
+    got = torch.gather(lb.float(), 1, idx_b.long())
+    assert torch.equal(got, torch.topk(lb.float(), k, dim=-1).values)
+
+
+@pytest.mark.parametrize("name", ["qwen3_next", "gpt_oss_20b"])
+def test_loader_matches_transformers_module(name):
+    """kernel(x, block) / kernel(x, mlp) against the transformers module the reference
+    benchmarks (op_eager), at reduced size, with the reference's verify() tolerance."""
+    from cernels_b200.hf_modules import build_module, reference_forward
+    from cernels_b200.registry import gpt_oss_moe_experts as go
+    from cernels_b200.registry import qwen3_next_moe_experts as qn
+    cfg = CONFIGS[name].scaled(tokens=256, experts=32 if name == "qwen3_next" else 8,
+                                hidden=512, inter=256, **({"shared_inter": 256} if name == "qwen3_next" else {}))
+    case = make_case(cfg, device=DEV)
+    kind, mod = build_module(case)
+    ref = reference_forward(kind, mod, case)
+    out = (qn.kernel if kind == "qwen3_next" else go.kernel)(case.x.unsqueeze(0), mod).squeeze(0)
+    close = torch.isclose(out.float(), ref.float(), atol=2e-2, rtol=2e-2)
+    # a bf16 tie in the router logits may pick a different expert for a token: allow <= 1% of rows
+    bad_rows = (~close).any(dim=1).float().mean().item()
+    assert bad_rows <= 0.01, bad_rows
