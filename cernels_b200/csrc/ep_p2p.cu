@@ -1,0 +1,466 @@
+// Expert-parallel dispatch / return over NVLink peer memory (no NCCL, no host sync).
+//
+// The reference is single-GPU; expert parallelism is this build's multi-GPU scheme. Each
+// rank owns one device window (cudaMalloc), mapped into every other rank's address space
+// with CUDA IPC:
+//   hdr[R]          one EpHeader per peer rank
+//   recv[R][cap][H] rows routed to this rank's experts, one slot per source rank
+//   back[cap][H]    expert outputs of this rank's own routed rows, written by their owners
+// One step (epoch e, all kernels on the caller's stream):
+//   ep_dispatch  source: per destination d, writes the per-expert row counts into
+//                d.hdr[me], copies its routed rows (gathered from x) into d.recv[me][i],
+//                then — after every CTA fenced — release-stores d.hdr[me].data_epoch = e
+//   ep_segments  destination: waits (acquire, bounded) for data_epoch == e from every source,
+//                builds the grouped-GEMM tables: group (s, local expert) -> rows in recv[s]
+//   2 x grouped_gemm_kernel on recv (tcgen05/TMA, in place)
+//   ep_return    destination: writes each result row into its source's back[seg_start + i],
+//                then release-stores s.hdr[me].result_epoch = e
+//   ep_combine   source: waits (acquire, bounded) for result_epoch == e from every destination,
+//                out[t] = bf16(sum_j w[t, j] * back[inv[t, j]]) in slot order
+// A rank starts step e+1 only after its combine of step e saw every destination's results,
+// and a destination signals results only after its GEMMs finished reading recv, so no slot
+// is overwritten while in use. Loads and stores are plain 16-byte accesses (no TMA and no
+// multicast on peer memory). Every wait gives up after kEpWaitNs and records a status.
+#include <cstdio>
+#include <cstring>
+
+#include "moe_internal.h"
+#include "sm100_primitives.cuh"
+
+namespace cernels {
+namespace {
+
+constexpr int kEpMaxRanks = 16;
+constexpr int kEpMaxLocalExperts = 512;
+constexpr unsigned long long kEpWaitNs = 5000000000ull;
+constexpr int kEpThreads = 256;
+
+struct __align__(256) EpHeader {
+  int32_t counts[kEpMaxLocalExperts];  // rows per local expert sent by this peer
+  int32_t seg_start;                   // first routed row of this segment at the source
+  int32_t n_rows;                      // rows in the segment
+  uint32_t data_epoch;                 // written by the source (destination's window)
+  uint32_t result_epoch;               // written by the destination (source's window)
+};
+
+__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// Bounded wait until *flag == epoch. Returns false (and records `code`) on timeout.
+__device__ bool wait_epoch(const uint32_t* flag, uint32_t epoch, int* status, int code) {
+  if (ld_acquire_sys(flag) == epoch) return true;
+  const unsigned long long t0 = global_timer_ns();
+  while (ld_acquire_sys(flag) != epoch) {
+    if (global_timer_ns() - t0 > kEpWaitNs) {
+      atomicCAS(status, 0, code);
+      return false;
+    }
+  }
+  return true;
+}
+
+__device__ __forceinline__ EpHeader* hdr_of(uint8_t* window, int peer) {
+  return reinterpret_cast<EpHeader*>(window) + peer;
+}
+
+struct EpGeometry {
+  int rank, world, local_experts, cap, hidden;
+  size_t recv_offset, back_offset;
+};
+
+// Marks this CTA done; the last CTA of the grid returns true (counter reset for the next launch).
+__device__ bool last_cta_done(unsigned* counter) {
+  __shared__ int last;
+  __threadfence_system();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const unsigned old = atomicAdd(counter, 1u);
+    last = old == gridDim.x - 1;
+    if (last) *counter = 0u;
+  }
+  __syncthreads();
+  return last != 0;
+}
+
+__global__ void __launch_bounds__(kEpThreads) ep_dispatch_kernel(uint8_t* const* __restrict__ peers, EpGeometry g,
+                                                                 const uint4* __restrict__ x,
+                                                                 const int* __restrict__ perm_token,
+                                                                 const int* __restrict__ offsets, uint32_t epoch,
+                                                                 unsigned* __restrict__ counter, int* status) {
+  const int El = g.local_experts;
+  if (blockIdx.x == 0) {
+    for (int i = threadIdx.x; i < g.world * El; i += blockDim.x) {
+      const int d = i / El, e = i - d * El;
+      hdr_of(peers[d], g.rank)->counts[e] = offsets[d * El + e + 1] - offsets[d * El + e];
+    }
+    for (int d = threadIdx.x; d < g.world; d += blockDim.x) {
+      EpHeader* h = hdr_of(peers[d], g.rank);
+      h->seg_start = offsets[d * El];
+      h->n_rows = offsets[(d + 1) * El] - offsets[d * El];
+    }
+  }
+  const int total = offsets[g.world * El];
+  const int vec = g.hidden / 8;
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+  const int n_warps = (gridDim.x * blockDim.x) >> 5;
+  for (int p = warp; p < total; p += n_warps) {
+    int d = 0;
+    while (d + 1 < g.world && offsets[(d + 1) * El] <= p) ++d;
+    const int i = p - offsets[d * El];
+    if (i >= g.cap) {  // cannot happen when cap >= tokens * topk; skip rather than overrun
+      if (lane == 0) atomicCAS(status, 0, kStatusTimeoutOther);
+      continue;
+    }
+    const uint4* src = x + static_cast<size_t>(perm_token[p]) * vec;
+    uint4* dst = reinterpret_cast<uint4*>(peers[d] + g.recv_offset) +
+                 (static_cast<size_t>(g.rank) * g.cap + i) * vec;
+    for (int v = lane; v < vec; v += 32) dst[v] = src[v];
+  }
+  if (last_cta_done(counter) && threadIdx.x < g.world)
+    st_release_sys(&hdr_of(peers[threadIdx.x], g.rank)->data_epoch, epoch);
+}
+
+// One CTA of 1024 threads: wait for every source, then group tables.
+__global__ void __launch_bounds__(1024) ep_segments_kernel(uint8_t* __restrict__ window, EpGeometry g, uint32_t epoch,
+                                                           int* __restrict__ offsets, int* __restrict__ group_rows,
+                                                           int* __restrict__ mtile_offsets, int* status) {
+  __shared__ int ok;
+  __shared__ int warp_tot[32];
+  __shared__ int carry;
+  if (threadIdx.x == 0) {
+    ok = 1;
+    carry = 0;
+  }
+  __syncthreads();
+  if (threadIdx.x < g.world)
+    if (!wait_epoch(&hdr_of(window, threadIdx.x)->data_epoch, epoch, status, kStatusTimeoutOther)) ok = 0;
+  __syncthreads();
+  fence_proxy_async_global();  // peer-written rows are read next by TMA (async proxy)
+  const int El = g.local_experts, G = g.world * El;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  for (int g0 = 0; g0 < G; g0 += 1024) {
+    const int gi = g0 + threadIdx.x;
+    int rows = 0, start = 0;
+    if (gi < G && ok) {
+      const int s = gi / El, e = gi - s * El;
+      const EpHeader* h = hdr_of(window, s);
+      for (int j = 0; j < e; ++j) start += h->counts[j];
+      rows = h->counts[e];
+      // clamp to this source's slot of the window
+      start = min(max(start, 0), g.cap);
+      rows = min(max(rows, 0), g.cap - start);
+      start += s * g.cap;
+    }
+    const int tiles = (rows + kBlockM - 1) / kBlockM;
+    // block exclusive scan of tiles
+    int incl = tiles;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int n = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += n;
+    }
+    if (lane == 31) warp_tot[warp] = incl;
+    __syncthreads();
+    if (warp == 0) {
+      const int wv = warp_tot[lane];
+      int wi = wv;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int n = __shfl_up_sync(0xffffffffu, wi, o);
+        if (lane >= o) wi += n;
+      }
+      warp_tot[lane] = wi - wv;
+    }
+    __syncthreads();
+    const int excl = carry + warp_tot[warp] + incl - tiles;
+    if (gi < G) {
+      offsets[gi] = start;
+      group_rows[gi] = rows;
+      mtile_offsets[gi] = excl;
+    }
+    __syncthreads();
+    if (threadIdx.x == 1023) carry = excl + tiles;
+    __syncthreads();
+  }
+  if (threadIdx.x == 0) {
+    mtile_offsets[G] = carry;
+    offsets[G] = g.world * g.cap;
+  }
+}
+
+__global__ void __launch_bounds__(kEpThreads) ep_return_kernel(uint8_t* const* __restrict__ peers, EpGeometry g,
+                                                               const uint4* __restrict__ rows, uint32_t epoch,
+                                                               unsigned* __restrict__ counter) {
+  uint8_t* own = peers[g.rank];
+  const int vec = g.hidden / 8;
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
+  const int n_warps = (gridDim.x * blockDim.x) >> 5;
+  for (int s = 0; s < g.world; ++s) {
+    const EpHeader* h = hdr_of(own, s);
+    // Headers come from another rank: clamp to the window so a bad value cannot overrun it.
+    const int base = min(max(h->seg_start, 0), g.cap);
+    const int n = min(max(h->n_rows, 0), min(g.cap - base, g.cap));
+    uint4* dst = reinterpret_cast<uint4*>(peers[s] + g.back_offset);
+    for (int i = warp; i < n; i += n_warps) {
+      const uint4* src = rows + (static_cast<size_t>(s) * g.cap + i) * vec;
+      uint4* o = dst + static_cast<size_t>(base + i) * vec;
+      for (int v = lane; v < vec; v += 32) o[v] = src[v];
+    }
+  }
+  if (last_cta_done(counter) && threadIdx.x < g.world)
+    st_release_sys(&hdr_of(peers[threadIdx.x], g.rank)->result_epoch, epoch);
+}
+
+__global__ void __launch_bounds__(kEpThreads) ep_combine_kernel(uint8_t* __restrict__ window, EpGeometry g,
+                                                                uint32_t epoch, const int* __restrict__ inv,
+                                                                const float* __restrict__ weights, int tokens,
+                                                                int topk, uint4* __restrict__ out, int* status) {
+  __shared__ int ok;
+  if (threadIdx.x == 0) ok = 1;
+  __syncthreads();
+  if (threadIdx.x < g.world)
+    if (!wait_epoch(&hdr_of(window, threadIdx.x)->result_epoch, epoch, status, kStatusTimeoutOther)) ok = 0;
+  __syncthreads();
+  const uint4* back = reinterpret_cast<const uint4*>(window + g.back_offset);
+  const int vec = g.hidden / 8;
+  const int warps = blockDim.x >> 5;
+  for (int t = blockIdx.x * warps + (threadIdx.x >> 5); t < tokens; t += gridDim.x * warps) {
+    for (int v = threadIdx.x & 31; v < vec; v += 32) {
+      float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+      for (int j = 0; j < topk && ok; ++j) {
+        const int p = inv[static_cast<size_t>(t) * topk + j];
+        if (p < 0) continue;
+        const uint4 r = __ldcv(back + static_cast<size_t>(p) * vec + v);
+        const float w = weights[static_cast<size_t>(t) * topk + j];
+        const __nv_bfloat162* h2 = reinterpret_cast<const __nv_bfloat162*>(&r);
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          const float2 f = __bfloat1622float2(h2[q]);
+          acc[2 * q] = fmaf(w, f.x, acc[2 * q]);
+          acc[2 * q + 1] = fmaf(w, f.y, acc[2 * q + 1]);
+        }
+      }
+      uint4 o;
+      __nv_bfloat162* oh = reinterpret_cast<__nv_bfloat162*>(&o);
+#pragma unroll
+      for (int q = 0; q < 4; ++q) oh[q] = __floats2bfloat162_rn(acc[2 * q], acc[2 * q + 1]);
+      out[static_cast<size_t>(t) * vec + v] = o;
+    }
+  }
+}
+
+}  // namespace
+}  // namespace cernels
+
+using namespace cernels;
+
+struct cernels_ep_ctx {
+  EpGeometry geo;
+  int device;
+  size_t window_bytes;
+  uint8_t* window;
+  uint8_t* peers[kEpMaxRanks];
+  uint8_t** d_peers;
+  unsigned* d_counters;  // [0] dispatch, [1] return
+  int* d_status;
+  bool connected;
+};
+
+namespace {
+
+int rc_of(cudaError_t e) {
+  if (e == cudaSuccess) return CERNELS_OK;
+  std::fprintf(stderr, "cernels_b200 ep: CUDA error: %s\n", cudaGetErrorString(e));
+  return CERNELS_E_CUDA;
+}
+
+int ep_grid(int rows) {
+  const int sms = device_sm_count();
+  const int want = (rows + 7) / 8;  // 8 warps per CTA, a row per warp
+  return want < 1 ? 1 : (want < 2 * sms ? want : 2 * sms);
+}
+
+}  // namespace
+
+extern "C" {
+
+int cernels_ep_create(int32_t rank, int32_t world, int32_t hidden, int32_t local_experts, int32_t max_rows,
+                      void** ctx_out, void* handle_out) {
+  if (!ctx_out || !handle_out) return CERNELS_E_NULL;
+  if (world < 1 || world > kEpMaxRanks || rank < 0 || rank >= world) return CERNELS_E_INVALID_SHAPE;
+  if (hidden <= 0 || hidden % 8 || local_experts <= 0 || local_experts > kEpMaxLocalExperts || max_rows <= 0)
+    return CERNELS_E_INVALID_SHAPE;
+  if (world * local_experts > kMaxExperts) return CERNELS_E_UNSUPPORTED;
+  auto* c = new cernels_ep_ctx();
+  std::memset(c, 0, sizeof(*c));
+  cudaGetDevice(&c->device);
+  c->geo.rank = rank;
+  c->geo.world = world;
+  c->geo.local_experts = local_experts;
+  c->geo.cap = max_rows;
+  c->geo.hidden = hidden;
+  const size_t hdr = align_up(sizeof(EpHeader) * world, 1024);
+  const size_t row = static_cast<size_t>(hidden) * 2;
+  c->geo.recv_offset = hdr;
+  c->geo.back_offset = align_up(hdr + static_cast<size_t>(world) * max_rows * row, 1024);
+  c->window_bytes = c->geo.back_offset + static_cast<size_t>(max_rows) * row;
+  cudaError_t err = cudaMalloc(&c->window, c->window_bytes);
+  if (err == cudaSuccess) err = cudaMemset(c->window, 0, c->geo.recv_offset);
+  if (err == cudaSuccess) err = cudaMalloc(&c->d_peers, sizeof(uint8_t*) * kEpMaxRanks);
+  if (err == cudaSuccess) err = cudaMalloc(&c->d_counters, 2 * sizeof(unsigned) + sizeof(int));
+  if (err == cudaSuccess) err = cudaMemset(c->d_counters, 0, 2 * sizeof(unsigned) + sizeof(int));
+  if (err == cudaSuccess) err = cudaIpcGetMemHandle(reinterpret_cast<cudaIpcMemHandle_t*>(handle_out), c->window);
+  if (err != cudaSuccess) {
+    if (c->window) cudaFree(c->window);
+    if (c->d_peers) cudaFree(c->d_peers);
+    if (c->d_counters) cudaFree(c->d_counters);
+    delete c;
+    return rc_of(err);
+  }
+  c->d_status = reinterpret_cast<int*>(c->d_counters + 2);
+  c->peers[rank] = c->window;
+  *ctx_out = c;
+  return CERNELS_OK;
+}
+
+int cernels_ep_connect(void* ctx, const void* handles) {
+  auto* c = static_cast<cernels_ep_ctx*>(ctx);
+  if (!c || !handles) return CERNELS_E_NULL;
+  const auto* h = static_cast<const cudaIpcMemHandle_t*>(handles);
+  for (int r = 0; r < c->geo.world; ++r) {
+    if (r == c->geo.rank) continue;
+    void* p = nullptr;
+    const cudaError_t err = cudaIpcOpenMemHandle(&p, h[r], cudaIpcMemLazyEnablePeerAccess);
+    if (err != cudaSuccess) return rc_of(err);
+    c->peers[r] = static_cast<uint8_t*>(p);
+  }
+  const cudaError_t err =
+      cudaMemcpy(c->d_peers, c->peers, sizeof(uint8_t*) * kEpMaxRanks, cudaMemcpyHostToDevice);
+  if (err != cudaSuccess) return rc_of(err);
+  c->connected = true;
+  return CERNELS_OK;
+}
+
+int cernels_ep_destroy(void* ctx) {
+  auto* c = static_cast<cernels_ep_ctx*>(ctx);
+  if (!c) return CERNELS_OK;
+  for (int r = 0; r < c->geo.world; ++r)
+    if (r != c->geo.rank && c->peers[r]) cudaIpcCloseMemHandle(c->peers[r]);
+  cudaFree(c->window);
+  cudaFree(c->d_peers);
+  cudaFree(c->d_counters);
+  delete c;
+  return CERNELS_OK;
+}
+
+int cernels_ep_dispatch(void* ctx, const void* x, const int32_t* perm_token, const int32_t* offsets, int32_t rows,
+                        uint32_t epoch, void* stream) {
+  auto* c = static_cast<cernels_ep_ctx*>(ctx);
+  if (!c || !c->connected) return CERNELS_E_NULL;
+  if (rows > c->geo.cap) return CERNELS_E_UNSUPPORTED;
+  if (rows > 0 && (!x || !perm_token || !offsets)) return CERNELS_E_NULL;
+  if (x && (reinterpret_cast<uintptr_t>(x) & 15)) return CERNELS_E_ALIGNMENT;
+  ep_dispatch_kernel<<<ep_grid(rows), kEpThreads, 0, static_cast<cudaStream_t>(stream)>>>(
+      c->d_peers, c->geo, static_cast<const uint4*>(x), perm_token, offsets, epoch, c->d_counters, c->d_status);
+  return rc_of(cudaGetLastError());
+}
+
+int cernels_ep_experts_workspace_bytes(void* ctx, const cernels_moe_shape* shape, size_t* bytes) {
+  auto* c = static_cast<cernels_ep_ctx*>(ctx);
+  if (!c || !shape || !bytes) return CERNELS_E_NULL;
+  const size_t rows = static_cast<size_t>(c->geo.world) * c->geo.cap;
+  const size_t G = static_cast<size_t>(c->geo.world) * c->geo.local_experts;
+  size_t off = 0;
+  off = align_up(off, 256) + (G + 1) * 4 * 3;  // offsets, group rows, tile offsets
+  off = align_up(off, 256) + rows * shape->intermediate * 2;
+  off = align_up(off, 256) + rows * c->geo.hidden * 2;
+  *bytes = off + 256;
+  return CERNELS_OK;
+}
+
+int cernels_ep_experts(void* ctx, const cernels_moe_shape* shape, const void* gate_up_proj, const float* gate_up_bias,
+                       const void* down_proj, const float* down_bias, uint32_t epoch, void* workspace,
+                       size_t workspace_bytes, void* stream_ptr) {
+  auto* c = static_cast<cernels_ep_ctx*>(ctx);
+  if (!c || !c->connected || !shape || !gate_up_proj || !down_proj || !workspace) return CERNELS_E_NULL;
+  const cernels_moe_shape s = *shape;
+  if (s.hidden != c->geo.hidden || s.experts != c->geo.local_experts || s.intermediate <= 0 ||
+      s.intermediate % 8)
+    return CERNELS_E_INVALID_SHAPE;
+  size_t need = 0;
+  cernels_ep_experts_workspace_bytes(ctx, shape, &need);
+  if (workspace_bytes < need) return CERNELS_E_WORKSPACE;
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
+  const int G = c->geo.world * c->geo.local_experts;
+  const size_t rows = static_cast<size_t>(c->geo.world) * c->geo.cap;
+  uint8_t* base = static_cast<uint8_t*>(workspace);
+  int* offsets = reinterpret_cast<int*>(base);
+  int* group_rows = offsets + (G + 1);
+  int* mtile = group_rows + (G + 1);
+  size_t off = align_up((G + 1) * 4 * 3, 256);
+  __nv_bfloat16* glu = reinterpret_cast<__nv_bfloat16*>(base + off);
+  off = align_up(off + rows * s.intermediate * 2, 256);
+  __nv_bfloat16* down_out = reinterpret_cast<__nv_bfloat16*>(base + off);
+
+  ep_segments_kernel<<<1, 1024, 0, stream>>>(c->window, c->geo, epoch, offsets, group_rows, mtile, c->d_status);
+  cudaError_t err = cudaGetLastError();
+  if (err != cudaSuccess) return rc_of(err);
+  const bool gptoss = s.layout == CERNELS_LAYOUT_GPTOSS;
+  const int sms = device_sm_count();
+  GroupedGemmArgs g1{};
+  g1.a = reinterpret_cast<const __nv_bfloat16*>(c->window + c->geo.recv_offset);
+  g1.b = static_cast<const __nv_bfloat16*>(gate_up_proj);
+  g1.bias = gptoss ? gate_up_bias : nullptr;
+  g1.out = glu;
+  g1.offsets = offsets;
+  g1.mtile_offsets = mtile;
+  g1.group_rows = group_rows;
+  g1.status = c->d_status;
+  g1.rows = static_cast<int>(rows);
+  g1.experts = G;
+  g1.k = s.hidden;
+  g1.n = 2 * s.intermediate;
+  g1.out_cols = s.intermediate;
+  g1.weight_experts = s.experts;
+  if ((err = launch_grouped_gemm(gptoss ? kGateUpGptOss : kGateUpLinear, g1, sms, stream)) != cudaSuccess)
+    return rc_of(err);
+  GroupedGemmArgs g2 = g1;
+  g2.a = glu;
+  g2.b = static_cast<const __nv_bfloat16*>(down_proj);
+  g2.bias = gptoss ? down_bias : nullptr;
+  g2.out = down_out;
+  g2.k = s.intermediate;
+  g2.n = s.hidden;
+  g2.out_cols = s.hidden;
+  if ((err = launch_grouped_gemm(gptoss ? kDownGptOss : kDownLinear, g2, sms, stream)) != cudaSuccess)
+    return rc_of(err);
+  ep_return_kernel<<<ep_grid(static_cast<int>(c->geo.cap)), kEpThreads, 0, stream>>>(
+      c->d_peers, c->geo, reinterpret_cast<const uint4*>(down_out), epoch, c->d_counters + 1);
+  return rc_of(cudaGetLastError());
+}
+
+int cernels_ep_combine(void* ctx, const int32_t* inv, const float* weights, int32_t tokens, int32_t topk, void* out,
+                       uint32_t epoch, void* stream) {
+  auto* c = static_cast<cernels_ep_ctx*>(ctx);
+  if (!c || !c->connected) return CERNELS_E_NULL;
+  if (tokens < 0 || topk <= 0) return CERNELS_E_INVALID_SHAPE;
+  if (tokens > 0 && (!inv || !weights || !out)) return CERNELS_E_NULL;
+  const int blocks = tokens > 0 ? ep_grid(tokens) : 1;
+  ep_combine_kernel<<<blocks, kEpThreads, 0, static_cast<cudaStream_t>(stream)>>>(
+      c->window, c->geo, epoch, inv, weights, tokens, topk, static_cast<uint4*>(out), c->d_status);
+  return rc_of(cudaGetLastError());
+}
+
+int cernels_ep_status(void* ctx, int* status) {
+  auto* c = static_cast<cernels_ep_ctx*>(ctx);
+  if (!c || !status) return CERNELS_E_NULL;
+  return rc_of(cudaMemcpy(status, c->d_status, sizeof(int), cudaMemcpyDeviceToHost));
+}
+
+}  // extern "C"

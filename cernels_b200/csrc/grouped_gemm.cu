@@ -232,7 +232,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const TileCoord c = decode_tile(t, n_tiles, s_mt, experts);
       const int e = c.expert % args.weight_experts;  // weight slab (bias row) of this row group
       const int row_begin = args.offsets[c.expert];
-      const int rows_e = args.offsets[c.expert + 1] - row_begin;
+      const int rows_e = args.group_rows ? args.group_rows[c.expert] : args.offsets[c.expert + 1] - row_begin;
       const int local_row = c.m_tile * BM + quarter * 32 + lane;
       const bool row_ok = local_row < rows_e;
       const size_t grow = static_cast<size_t>(row_begin + local_row);

@@ -79,6 +79,7 @@ struct GroupedGemmArgs {
   int n;                       // columns of the weight product (2F or H)
   int out_cols;                // F for gate/up, H for down
   int weight_experts;          // experts in the weight tensors; row group g uses expert g % weight_experts
+  const int* group_rows;       // optional [groups]: rows of group g (default offsets[g+1] - offsets[g])
 };
 
 enum GemmMode : int {

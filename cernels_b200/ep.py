@@ -74,11 +74,79 @@ def cuda_backend(layout: int, w1: torch.Tensor, w2: torch.Tensor, b1=None, b2=No
     return Backend(route=ops.route, gather=ops.gather_rows, experts=experts, combine=ops.combine_rows)
 
 
+class P2PTransport:
+    """Device-side dispatch / return over NVLink peer memory (include/cernels_b200.h,
+    cernels_ep_*): one IPC-shared window per rank, no NCCL and no host sync per step."""
+
+    def __init__(self, rank: int, world: int, hidden: int, local_experts: int, max_rows: int, device, group=None):
+        import ctypes
+
+        from . import _lib
+
+        self._lib = _lib
+        lib = _lib.load()
+        self.ctx = ctypes.c_void_p()
+        handle = ctypes.create_string_buffer(64)
+        with torch.cuda.device(device):
+            _lib.check(lib.cernels_ep_create(rank, world, hidden, local_experts, max_rows, ctypes.byref(self.ctx),
+                                             handle), "cernels_ep_create")
+            handles = [None] * world
+            dist.all_gather_object(handles, handle.raw, group=group)
+            _lib.check(lib.cernels_ep_connect(self.ctx, b"".join(handles)), "cernels_ep_connect")
+        dist.barrier(group=group)
+        self.device = device
+        self.max_rows = max_rows
+        self.epoch = 0
+        self._ws = None
+
+    def status(self) -> int:
+        import ctypes
+
+        st = ctypes.c_int(0)
+        self._lib.check(self._lib.load().cernels_ep_status(self.ctx, ctypes.byref(st)), "cernels_ep_status")
+        return int(st.value)
+
+    def step(self, x, perm_token, offsets, inv, w, weights, shape):
+        """dispatch -> grouped experts -> return -> combine for one batch; returns [T, H] bf16."""
+        import ctypes
+
+        lib = self._lib.load()
+        T, k = w.shape
+        if T * k > self.max_rows:
+            raise RuntimeError(f"expert-parallel window holds {self.max_rows} routed rows, batch has {T * k}")
+        layout, w1, b1, w2, b2 = weights
+        self.epoch += 1
+        stream = torch.cuda.current_stream(self.device).cuda_stream
+        ptr = lambda t: None if t is None else t.data_ptr()  # noqa: E731
+        self._lib.check(lib.cernels_ep_dispatch(self.ctx, x.data_ptr(), perm_token.data_ptr(), offsets.data_ptr(),
+                                                T * k, self.epoch, stream), "cernels_ep_dispatch")
+        n = ctypes.c_size_t(0)
+        self._lib.check(lib.cernels_ep_experts_workspace_bytes(self.ctx, ctypes.byref(shape), ctypes.byref(n)),
+                        "cernels_ep_experts_workspace_bytes")
+        if self._ws is None or self._ws.numel() < n.value:
+            self._ws = torch.empty(n.value, dtype=torch.uint8, device=self.device)
+        self._lib.check(lib.cernels_ep_experts(self.ctx, ctypes.byref(shape), w1.data_ptr(), ptr(b1), w2.data_ptr(),
+                                               ptr(b2), self.epoch, self._ws.data_ptr(), n.value, stream),
+                        "cernels_ep_experts")
+        out = torch.empty(T, x.shape[1], dtype=x.dtype, device=x.device)
+        self._lib.check(lib.cernels_ep_combine(self.ctx, inv.data_ptr(), w.data_ptr(), T, k, out.data_ptr(),
+                                               self.epoch, stream), "cernels_ep_combine")
+        return out
+
+    def __del__(self):
+        try:
+            if self.ctx:
+                self._lib.load().cernels_ep_destroy(self.ctx)
+        except Exception:
+            pass
+
+
 class ExpertParallelMoe:
     """EP forward over a process group; weights of the local expert slice only."""
 
     def __init__(self, experts: int, topk: int, rank: int, world: int, router: Callable, backend: Backend,
-                 shared: Callable | None = None, group=None, chunks: int | None = None):
+                 shared: Callable | None = None, group=None, chunks: int | None = None,
+                 local_weights: tuple | None = None, transport: str = "auto"):
         self.E = experts
         self.k = topk
         self.rank = rank
@@ -89,8 +157,12 @@ class ExpertParallelMoe:
         self.shared = shared
         self.group = group
         self.chunks = chunks  # None: chosen from the row count
-        # route(3) + gather(1) + combine(1) + per chunk grouped experts (scan + 2 GEMMs); + 7 shared
-        self.launches_per_step = 5 + 3 * 4 + (7 if shared is not None else 0)
+        # (layout, w1, b1, w2, b2) of the local expert slice; needed by the peer-memory transport
+        self.local_weights = local_weights
+        self.transport = transport  # "p2p" (CUDA peer memory), "nccl", or "auto"
+        self._p2p = None
+        # router tail(1) + route(3) + dispatch(1) + segments(1) + 2 GEMMs + return(1) + combine(1); + 8 shared
+        self.launches_per_step = 10 + (8 if shared is not None else 0)
 
     # ------------------------------------------------------------ construction
     @classmethod
@@ -106,27 +178,30 @@ class ExpertParallelMoe:
             b1 = ex.gate_up_proj_bias.data[e0:e1].float().contiguous()
             b2 = ex.down_proj_bias.data[e0:e1].float().contiguous()
             backend = cuda_backend(LAYOUT_GPTOSS, w1, w2, b1, b2)
+            local = (LAYOUT_GPTOSS, w1, b1, w2, b2)
 
             from .registry import gpt_oss_moe_experts as go
 
             def router(x):
                 return go.route(x, module)
 
-            return cls(E, int(module.router.top_k), rank, world, router, backend, None, group)
+            return cls(E, int(module.router.top_k), rank, world, router, backend, None, group, local_weights=local)
         if kind == "qwen3_next":
             from .registry import qwen3_next_moe_experts as qn
 
             ex = module.experts
             E = ex.gate_up_proj.shape[0]
             e0, e1 = expert_shard(E, rank, world)
-            backend = cuda_backend(LAYOUT_LINEAR, ex.gate_up_proj.data[e0:e1].contiguous(),
-                                   ex.down_proj.data[e0:e1].contiguous())
+            w1 = ex.gate_up_proj.data[e0:e1].contiguous()
+            w2 = ex.down_proj.data[e0:e1].contiguous()
+            backend = cuda_backend(LAYOUT_LINEAR, w1, w2)
+            local = (LAYOUT_LINEAR, w1, None, w2, None)
 
             def router(x):
                 return qn.route(x, module)
 
             return cls(E, int(module.gate.top_k), rank, world, router, backend, lambda x: qn.shared_expert(x, module),
-                       group)
+                       group, local_weights=local)
         raise ValueError(f"expert parallelism is not used for {kind}")
 
     # ------------------------------------------------------------ forward
@@ -147,7 +222,40 @@ class ExpertParallelMoe:
         # calls cost more than the overlap gains at 2 ranks (measured); callers can opt in.
         return 1 if self.chunks is None else max(1, int(self.chunks))
 
+    def use_p2p(self, x: torch.Tensor) -> bool:
+        if self.transport == "nccl" or not x.is_cuda or self.local_weights is None:
+            return False
+        return True
+
     def forward(self, x: torch.Tensor) -> torch.Tensor:
+        if self.use_p2p(x):
+            return self.forward_p2p(x)
+        return self.forward_nccl(x)
+
+    def forward_p2p(self, x: torch.Tensor) -> torch.Tensor:
+        from . import _lib
+
+        with torch.no_grad():
+            idx, w = self.router(x)
+            idx = idx.to(torch.int32).contiguous()
+            w = w.float().contiguous()
+            offsets, perm_token, _perm_weight, inv = self.backend.route(idx, w, self.E)
+            if self._p2p is None:
+                # window capacity: the most routed rows any rank can send (all ranks agree)
+                cap = torch.tensor([idx.numel()], dtype=torch.int64, device=x.device)
+                dist.all_reduce(cap, op=dist.ReduceOp.MAX, group=self.group)
+                self._p2p = P2PTransport(self.rank, self.world, x.shape[1], self.E // self.world, int(cap.item()),
+                                         x.device, self.group)
+            layout, w1, b1, w2, b2 = self.local_weights
+            F = w1.shape[1] // 2 if layout == 0 else w1.shape[2] // 2
+            shape = _lib.MoeShape(int(self._p2p.max_rows), int(x.shape[1]), int(self.E // self.world), int(F), 1,
+                                  int(layout))
+            out = self._p2p.step(x.contiguous(), perm_token, offsets, inv, w, self.local_weights, shape)
+            if self.shared is not None:
+                out = out + self.shared(x)
+            return out
+
+    def forward_nccl(self, x: torch.Tensor) -> torch.Tensor:
         R, E, k = self.world, self.E, self.k
         per = E // R
         dev = x.device

@@ -3,8 +3,9 @@
  *
  * Every entry point takes plain device pointers, sizes and a CUDA stream (passed as
  * void*), launches asynchronously on that stream and returns 0 or a CERNELS_E_* code.
- * Nothing here allocates device memory: scratch comes from a caller-provided workspace
- * whose size cernels_moe_workspace_bytes() reports. No entry point synchronises the
+ * Apart from cernels_ep_create (the expert-parallel window), nothing here allocates device
+ * memory: scratch comes from a caller-provided workspace whose size
+ * cernels_moe_workspace_bytes() reports. No entry point synchronises the
  * stream or reads device memory on the host, so a call can be captured in a CUDA graph.
  *
  * Tensor conventions (all contiguous, row-major):
@@ -159,6 +160,33 @@ int cernels_moe_experts_profiled(const cernels_moe_shape* shape, const void* x, 
 int cernels_moe_experts_decode_noalloc(const cernels_moe_shape* shape, const void* x, const void* gate_up_proj,
                                        const float* gate_up_bias, const void* down_proj, const float* down_bias,
                                        const int32_t* indices, const float* weights, void* out, void* stream);
+
+/* ---- Expert parallelism over NVLink peer memory (no counterpart in the reference, which is
+ * single-GPU). One context per rank (one process per GPU): a device window holding a receive
+ * slot per source rank ([world][max_rows][H] bf16), a return region ([max_rows][H]) and small
+ * headers, shared with the other ranks through CUDA IPC. Per step, with a step counter `epoch`
+ * that every rank increments identically (starting at 1):
+ *   cernels_ep_dispatch  routed rows (x[perm_token[p]], p < offsets[E]) -> owners' windows
+ *   cernels_ep_experts   waits for all sources, grouped GEMMs on the received rows, returns
+ *                        each result row into its source's window
+ *   cernels_ep_combine   waits for all results, out[t] = bf16(sum_j w[t,j] * row[inv[t,j]])
+ * offsets/perm_token/inv come from cernels_moe_route over the GLOBAL expert ids (experts are
+ * sharded contiguously: rank r owns [r*El, (r+1)*El)). Waits inside the kernels give up after
+ * 5 s and record a nonzero status (cernels_ep_status). */
+#define CERNELS_EP_HANDLE_BYTES 64
+int cernels_ep_create(int32_t rank, int32_t world, int32_t hidden, int32_t local_experts, int32_t max_rows,
+                      void** ctx, void* ipc_handle_out);
+int cernels_ep_connect(void* ctx, const void* ipc_handles /* world * CERNELS_EP_HANDLE_BYTES, rank order */);
+int cernels_ep_destroy(void* ctx);
+int cernels_ep_dispatch(void* ctx, const void* x, const int32_t* perm_token, const int32_t* offsets, int32_t rows,
+                        uint32_t epoch, void* stream);
+int cernels_ep_experts_workspace_bytes(void* ctx, const cernels_moe_shape* shape, size_t* bytes);
+int cernels_ep_experts(void* ctx, const cernels_moe_shape* shape, const void* gate_up_proj, const float* gate_up_bias,
+                       const void* down_proj, const float* down_bias, uint32_t epoch, void* workspace,
+                       size_t workspace_bytes, void* stream);
+int cernels_ep_combine(void* ctx, const int32_t* inv, const float* weights, int32_t tokens, int32_t topk, void* out,
+                       uint32_t epoch, void* stream);
+int cernels_ep_status(void* ctx, int* status);
 
 /* Device status word of the last call that used this workspace (0 = ok; nonzero when a
  * bounded wait inside a kernel gave up). Reads device memory: synchronises `stream`. */

@@ -24,7 +24,7 @@ def _free_port():
     return p
 
 
-def _worker(rank, world, port, cfg_name, tokens, q):
+def _worker(rank, world, port, cfg_name, tokens, transport, q):
     import datetime
 
     import torch.distributed as dist
@@ -46,18 +46,24 @@ def _worker(rank, world, port, cfg_name, tokens, q):
         case = make_case(cfg, device=f"cuda:{rank}")
         kind, module = build_module(case)
         moe = ep.ExpertParallelMoe.from_module(kind, module, rank, world)
+        moe.transport = transport
         shard = ep.token_shard(cfg.tokens, rank, world)
         out = moe.forward(case.x[shard].contiguous())
+        out2 = moe.forward(case.x[shard].contiguous())  # a second step (reused windows / epochs)
         full = (go.kernel if kind == "gpt_oss" else qn.kernel)(case.x.unsqueeze(0), module).squeeze(0)
         torch.cuda.synchronize()
-        err = O.rel_err(out.float().cpu().numpy(), full[shard].float().cpu().numpy())
+        err = max(O.rel_err(out.float().cpu().numpy(), full[shard].float().cpu().numpy()),
+                  O.rel_err(out2.float().cpu().numpy(), full[shard].float().cpu().numpy()))
+        if transport == "p2p":
+            assert moe._p2p is not None and moe._p2p.status() == 0
         q.put((rank, err))
     finally:
         dist.destroy_process_group()
 
 
+@pytest.mark.parametrize("transport", ["p2p", "nccl"])
 @pytest.mark.parametrize("cfg_name,tokens", [("gpt_oss_20b", 2048), ("qwen3_next", 1024)])
-def test_ep_matches_single_gpu(cfg_name, tokens):
+def test_ep_matches_single_gpu(cfg_name, tokens, transport):
     world = torch.cuda.device_count()
     if world < 2:
         pytest.skip("needs 2 or more GPUs")
@@ -65,7 +71,7 @@ def test_ep_matches_single_gpu(cfg_name, tokens):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, world, port, cfg_name, tokens, q)) for r in range(world)]
+    procs = [ctx.Process(target=_worker, args=(r, world, port, cfg_name, tokens, transport, q)) for r in range(world)]
     for p in procs:
         p.start()
     errs = dict(q.get(timeout=600) for _ in range(world))
