@@ -25,7 +25,6 @@ import argparse
 import json
 import os
 import statistics
-import subprocess
 import sys
 import time
 
@@ -71,55 +70,65 @@ def init_dist(world: int, backend: str):
 
 # ---------------------------------------------------------------- clocks
 class ClockSampler:
-    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    """Samples SM clock, power and clock-event reasons of this rank's GPU through NVML (read
+    only) every 5 ms on a background thread while the timed region runs."""
 
-    def __init__(self, gpu_index: int):
-        self.gpu = gpu_index
-        self.proc = None
-        self.path = os.path.join(ROOT, "gpurun_out", f"clocks_rank{gpu_index}.csv")
+    REASONS = {"hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20, "hw_thermal_slowdown": 0x40,
+               "sw_power_cap": 0x4}
+
+    def __init__(self, cuda_index: int):
+        self.cuda_index = cuda_index
+        self.samples = []
+        self.max_mhz = None
+        self._stop = None
+        self._thread = None
+        self.error = None
 
     def __enter__(self):
+        import threading
+
         try:
-            os.makedirs(os.path.dirname(self.path), exist_ok=True)
-            self.fh = open(self.path, "w")
-            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.gpu), f"--query-gpu={self.QUERY}",
-                                          "--format=csv,noheader,nounits", "-lms", "200"],
-                                         stdout=self.fh, stderr=subprocess.DEVNULL)
-        except Exception:
-            self.proc = None
+            import pynvml
+            import torch
+
+            pynvml.nvmlInit()
+            bus = torch.cuda.get_device_properties(self.cuda_index).pci_bus_id
+            try:
+                h = pynvml.nvmlDeviceGetHandleByPciBusId(bus)
+            except Exception:
+                h = pynvml.nvmlDeviceGetHandleByIndex(self.cuda_index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM)
+            self._stop = threading.Event()
+
+            def run():
+                while not self._stop.is_set():
+                    try:
+                        mhz = pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM)
+                        pw = pynvml.nvmlDeviceGetPowerUsage(h) / 1000.0
+                        rs = pynvml.nvmlDeviceGetCurrentClocksEventReasons(h)
+                        self.samples.append((mhz, pw, rs))
+                    except Exception as e:  # keep the benchmark running
+                        self.error = str(e)
+                    self._stop.wait(0.005)
+
+            self._thread = threading.Thread(target=run, daemon=True)
+            self._thread.start()
+        except Exception as e:
+            self.error = f"nvml unavailable: {e}"
         return self
 
     def __exit__(self, *exc):
-        if self.proc is not None:
-            self.proc.terminate()
-            try:
-                self.proc.wait(timeout=5)
-            except Exception:
-                self.proc.kill()
-            self.fh.close()
+        if self._thread is not None:
+            self._stop.set()
+            self._thread.join(timeout=2)
 
     def summary(self):
-        if self.proc is None:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
-        rows = []
-        with open(self.path) as f:
-            for line in f:
-                parts = [s.strip() for s in line.split(",")]
-                if len(parts) < 9:
-                    continue
-                try:
-                    rows.append((float(parts[1]), float(parts[2]), float(parts[3]), parts[4:]))
-                except ValueError:
-                    continue
-        if not rows:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
-        loaded = [r for r in rows if r[2] > 300.0] or rows
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        reasons = sorted({names[i] for r in loaded for i, v in enumerate(r[3][1:5]) if v.lower() == "active"})
-        return {"sm_mhz": statistics.median(r[0] for r in loaded), "sm_max_mhz": max(r[1] for r in rows),
-                "reasons": reasons, "samples": len(loaded)}
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": [self.error or "no samples"]}
+        loaded = [s for s in self.samples if s[1] > 300.0] or self.samples
+        reasons = sorted({n for s in loaded for n, bit in self.REASONS.items() if s[2] & bit})
+        return {"sm_mhz": statistics.median(s[0] for s in loaded), "sm_max_mhz": self.max_mhz, "reasons": reasons,
+                "samples": len(loaded), "power_w_median": round(statistics.median(s[1] for s in loaded), 1)}
 
 
 # ---------------------------------------------------------------- workload
