@@ -27,15 +27,19 @@ namespace cernels {
 namespace {
 
 constexpr int BM = kBlockM;  // 128
-constexpr int BN = 256;
+constexpr int BN_MAX = 256;  // widest N tile; 192 is used when it divides N and 256 does not
 constexpr int BK = 64;       // 64 bf16 = 128 bytes = one swizzle row
 constexpr int kStages = 4;
 constexpr int kABytes = BM * BK * 2;  // 16 KB
-constexpr int kBBytes = BN * BK * 2;  // 32 KB
+constexpr int kBBytesMax = BN_MAX * BK * 2;  // 32 KB
+constexpr int kBoxBytes = 64 * BK * 2;         // one 64-column N-major box [64 K rows x 128 B]
+constexpr int kAccStride = 256;                // TMEM column offset between the two accumulators
 constexpr int kThreads = 192;
 constexpr int kTmemCols = 512;
 constexpr int kBarrierBytes = 256;
-constexpr size_t kSmemFixed = static_cast<size_t>(kStages) * (kABytes + kBBytes) + kBarrierBytes;
+__host__ __device__ constexpr size_t smem_fixed(int bn) {
+  return static_cast<size_t>(kStages) * (kABytes + bn * BK * 2) + kBarrierBytes;
+}
 
 constexpr float kGptOssLimit = 7.0f;
 constexpr float kGptOssAlpha = 1.702f;
@@ -43,10 +47,10 @@ constexpr float kGptOssAlpha = 1.702f;
 __host__ __device__ constexpr bool mode_is_gptoss(int mode) { return mode == kGateUpGptOss || mode == kDownGptOss; }
 
 // Number of n-tiles of one expert's output.
-__host__ __device__ inline int n_tiles_for(int mode, int n) {
+__host__ __device__ inline int n_tiles_for(int mode, int n, int bn) {
   // Linear gate/up pairs 128 gate rows with 128 up rows per tile: n = 2F, F/128 tiles.
   if (mode == kGateUpLinear) return (n / 2 + 127) / 128;
-  return (n + BN - 1) / BN;
+  return (n + bn - 1) / bn;
 }
 
 struct TileCoord {
@@ -86,7 +90,7 @@ __device__ __forceinline__ float gptoss_glu(float gate, float up) {
   return (up + 1.0f) * glu;
 }
 
-template <int kMode>
+template <int kMode, int BN>
 __global__ void __launch_bounds__(kThreads, 1)
     grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
                         GroupedGemmArgs args) {
@@ -94,6 +98,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* smem_a = smem;
   uint8_t* smem_b = smem + kStages * kABytes;
+  constexpr int kBBytes = BN * BK * 2;
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + kStages * (kABytes + kBBytes));
   uint64_t* full_bar = bars;                  // [kStages]
   uint64_t* empty_bar = bars + kStages;       // [kStages]
@@ -108,7 +113,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int lane = threadIdx.x & 31;
 
   for (int i = threadIdx.x; i <= experts; i += blockDim.x) s_mt[i] = args.mtile_offsets[i];
-  const int n_tiles = n_tiles_for(kMode, args.n);
+  const int n_tiles = n_tiles_for(kMode, args.n, BN);
   __syncthreads();
   const int total_tiles = s_mt[experts] * n_tiles;
   if (static_cast<int>(blockIdx.x) >= total_tiles) return;  // uniform per CTA
@@ -165,10 +170,10 @@ __global__ void __launch_bounds__(kThreads, 1)
           } else if constexpr (kMode == kDownLinear) {
             tma_load_3d(b_dst, &tmap_b, &full_bar[stage], kb * BK, c.n_tile * BN, we, kCacheEvictNormal);
           } else {
-            // N-major weights: four 64-column boxes, each [64 K rows x 128 bytes].
+            // N-major weights: BN/64 boxes of 64 columns, each [64 K rows x 128 bytes].
 #pragma unroll
-            for (int j = 0; j < 4; ++j)
-              tma_load_3d(b_dst + j * (kBBytes / 4), &tmap_b, &full_bar[stage], c.n_tile * BN + 64 * j, kb * BK,
+            for (int j = 0; j < BN / 64; ++j)
+              tma_load_3d(b_dst + j * kBoxBytes, &tmap_b, &full_bar[stage], c.n_tile * BN + 64 * j, kb * BK,
                           we, kCacheEvictNormal);
           }
           if (++stage == kStages) {
@@ -191,7 +196,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const uint32_t acc_phase = (local >> 1) & 1;
         if (!mbar_wait_bounded(&tempty_bar[acc], acc_phase ^ 1u, args.status, kStatusTimeoutMma, abort_flag)) break;
         tc_fence_after();
-        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * BN);
+        const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * kAccStride);
         for (int kb = 0; kb < k_blocks; ++kb) {
           if (!mbar_wait_bounded(&full_bar[stage], phase, args.status, kStatusTimeoutMma, abort_flag)) {
             ok = false;
@@ -205,7 +210,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             const uint64_t a_desc = make_smem_desc_sw128(a_addr + kk * 32, 16, 1024);
             uint64_t b_desc;
             if constexpr (mode_is_gptoss(kMode)) {
-              b_desc = make_smem_desc_sw128(b_addr + kk * 2048, kBBytes / 4, 1024);
+              b_desc = make_smem_desc_sw128(b_addr + kk * 2048, kBoxBytes, 1024);
             } else {
               b_desc = make_smem_desc_sw128(b_addr + kk * 32, 16, 1024);
             }
@@ -236,7 +241,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int local_row = c.m_tile * BM + quarter * 32 + lane;
       const bool row_ok = local_row < rows_e;
       const size_t grow = static_cast<size_t>(row_begin + local_row);
-      const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(acc * BN);
+      const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(acc * kAccStride);
 
       if constexpr (kMode == kGateUpLinear) {
         const int F = args.out_cols;
@@ -343,7 +348,7 @@ bool encode_map(CUtensorMap* map, const void* ptr, int rank, const uint64_t* dim
   return r == CUDA_SUCCESS;
 }
 
-template <int kMode>
+template <int kMode, int BN>
 cudaError_t launch_mode(const GroupedGemmArgs& args, int num_sms, cudaStream_t stream) {
   CUtensorMap map_a, map_b;
   {
@@ -366,31 +371,41 @@ cudaError_t launch_mode(const GroupedGemmArgs& args, int num_sms, cudaStream_t s
     const uint32_t box[3] = {64, BK, 1};
     if (!encode_map(&map_b, args.b, 3, dims, strides, box)) return cudaErrorInvalidValue;
   }
-  const size_t smem = kSmemFixed + 1024 + static_cast<size_t>(args.experts + 1) * sizeof(int);
+  const size_t smem = smem_fixed(BN) + 1024 + static_cast<size_t>(args.experts + 1) * sizeof(int);
   static bool attr_set = false;
   if (!attr_set) {
-    cudaError_t err = cudaFuncSetAttribute(grouped_gemm_kernel<kMode>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                           static_cast<int>(kSmemFixed + 1024 + (kMaxExperts + 1) * sizeof(int)));
+    cudaError_t err =
+        cudaFuncSetAttribute(grouped_gemm_kernel<kMode, BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             static_cast<int>(smem_fixed(BN) + 1024 + (kMaxExperts + 1) * sizeof(int)));
     if (err != cudaSuccess) return err;
     attr_set = true;
   }
-  const int n_tiles = n_tiles_for(kMode, args.n);
+  const int n_tiles = n_tiles_for(kMode, args.n, BN);
   const long long max_mtiles = (static_cast<long long>(args.rows) + BM - 1) / BM + args.experts;
   const long long max_tiles = max_mtiles * n_tiles;
   const int grid = static_cast<int>(max_tiles < num_sms ? max_tiles : num_sms);
   if (grid <= 0) return cudaSuccess;
-  grouped_gemm_kernel<kMode><<<grid, kThreads, smem, stream>>>(map_a, map_b, args);
+  grouped_gemm_kernel<kMode, BN><<<grid, kThreads, smem, stream>>>(map_a, map_b, args);
   return cudaGetLastError();
 }
 
 }  // namespace
 
 cudaError_t launch_grouped_gemm(GemmMode mode, const GroupedGemmArgs& args, int num_sms, cudaStream_t stream) {
+  // 192-wide N tiles when they divide N exactly and 256 does not (e.g. N = 2880, 5760):
+  // no padded last tile.
+  const bool narrow = args.n % 256 != 0 && args.n % 192 == 0;
   switch (mode) {
-    case kGateUpLinear: return launch_mode<kGateUpLinear>(args, num_sms, stream);
-    case kGateUpGptOss: return launch_mode<kGateUpGptOss>(args, num_sms, stream);
-    case kDownLinear: return launch_mode<kDownLinear>(args, num_sms, stream);
-    case kDownGptOss: return launch_mode<kDownGptOss>(args, num_sms, stream);
+    case kGateUpLinear: return launch_mode<kGateUpLinear, 256>(args, num_sms, stream);
+    case kGateUpGptOss:
+      return narrow ? launch_mode<kGateUpGptOss, 192>(args, num_sms, stream)
+                    : launch_mode<kGateUpGptOss, 256>(args, num_sms, stream);
+    case kDownLinear:
+      return narrow ? launch_mode<kDownLinear, 192>(args, num_sms, stream)
+                    : launch_mode<kDownLinear, 256>(args, num_sms, stream);
+    case kDownGptOss:
+      return narrow ? launch_mode<kDownGptOss, 192>(args, num_sms, stream)
+                    : launch_mode<kDownGptOss, 256>(args, num_sms, stream);
   }
   return cudaErrorInvalidValue;
 }
