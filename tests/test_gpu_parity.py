@@ -344,3 +344,21 @@ def test_loader_matches_transformers_module(name):
     # a bf16 tie in the router logits may pick a different expert for a token: allow <= 1% of rows
     bad_rows = (~close).any(dim=1).float().mean().item()
     assert bad_rows <= 0.01, bad_rows
+
+
+def test_host_pipeline_matches_direct_call():
+    """cernels_b200.pipeline.HostPipeline: chunked host->device->host run equals one call."""
+    from cernels_b200.pipeline import HostPipeline
+    g = torch.Generator().manual_seed(3)
+    T, H, E, F, k = 1000, 512, 16, 256, 4
+    x = torch.randn(T, H, generator=g).to(torch.bfloat16)
+    w1 = (torch.randn(E, 2 * F, H, generator=g) * 0.05).to(torch.bfloat16).to(DEV)
+    w2 = (torch.randn(E, H, F, generator=g) * 0.05).to(torch.bfloat16).to(DEV)
+    idx = torch.stack([torch.randperm(E, generator=g)[:k] for _ in range(T)]).to(torch.int32)
+    w = torch.rand(T, k, generator=g)
+    step = lambda xx, ii, ww: ops.cohere2_moe_experts(xx, w1, w2, ii, ww, k)  # noqa: E731
+    direct = step(x.to(DEV), idx.to(DEV), w.to(DEV)).cpu()
+    out = torch.empty(T, H, dtype=torch.bfloat16).pin_memory()
+    HostPipeline().run(step, [x.pin_memory(), idx.pin_memory(), w.pin_memory()], out, chunks=3)
+    torch.cuda.synchronize()
+    assert torch.equal(out, direct)
