@@ -28,6 +28,10 @@ import statistics
 import sys
 import time
 
+import faulthandler
+
+faulthandler.enable()  # a native crash prints the Python stack of every thread to stderr
+
 ROOT = os.path.dirname(os.path.abspath(__file__))
 if ROOT not in sys.path:
     sys.path.insert(0, ROOT)
@@ -445,6 +449,10 @@ def run_reference(args):
 
 
 # ---------------------------------------------------------------- our arm
+def log(msg: str) -> None:
+    print(f"[bench] {msg}", file=sys.stderr, flush=True)
+
+
 def run_ours(args):
     import torch
 
@@ -456,6 +464,7 @@ def run_ours(args):
     dist = init_dist(world, "nccl")
     import cernels_b200  # noqa: F401  (loads the CUDA library; raises if missing)
 
+    log("building workload")
     cfg, case, kind, module = build_workload(args, device, rank, world)
     step, inputs, launches = make_step(cfg, case, kind, module, world, rank)
     flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=device)
@@ -464,8 +473,10 @@ def run_ours(args):
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
+    log("timed region")
     with ClockSampler(local) as clocks:
         total_ms, per = time_device(step, inputs, args.steps, warmup, flush, graph=args.graph)
+    log(f"clock samples: {len(clocks.samples)} ({clocks.error})")
     torch.cuda.synchronize()
     if world > 1:
         t = torch.tensor([total_ms], device=device)
@@ -474,6 +485,7 @@ def run_ours(args):
         dist.barrier()
     # token-chunked copy/compute overlap for large single-GPU batches (EP steps are collective)
     e2e_chunks = 4 if (world == 1 and cfg.tokens >= 4096) else 1
+    log("e2e")
     e2e_ms, h2d, d2h = time_e2e(step, inputs, args.steps, warmup, flush, e2e_chunks)
     if world > 1:
         t = torch.tensor([e2e_ms], device=device)
@@ -490,8 +502,10 @@ def run_ours(args):
         if cfg.name == "decode":
             roof = decode_roofline(case, min(args.steps, 20))
         elif world == 1 or cfg.name not in EP_CONFIGS:
+            log("stage profile")
             roof = roofline(cfg, case, stage_profile(case, min(args.steps, 10)))
         if world == 1 and not args.no_cpu_baseline:
+            log("cpu baseline")
             cpu = cpu_oracle_baseline(case, args.cpu_sample_s)
     if rank == 0:
         line = {
