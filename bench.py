@@ -96,11 +96,18 @@ class ClockSampler:
             import torch
 
             pynvml.nvmlInit()
-            bus = torch.cuda.get_device_properties(self.cuda_index).pci_bus_id
-            try:
-                h = pynvml.nvmlDeviceGetHandleByPciBusId(bus)
-            except Exception:
-                h = pynvml.nvmlDeviceGetHandleByIndex(self.cuda_index)
+            # match this CUDA device to its NVML handle by PCI bus id (NVML order may differ)
+            want = str(torch.cuda.get_device_properties(self.cuda_index).pci_bus_id).lower()[-7:]
+            h = None
+            for i in range(pynvml.nvmlDeviceGetCount()):
+                cand = pynvml.nvmlDeviceGetHandleByIndex(i)
+                bus = pynvml.nvmlDeviceGetPciInfo(cand).busId
+                bus = bus.decode() if isinstance(bus, bytes) else str(bus)
+                if bus.lower()[-7:] == want:
+                    h = cand
+                    break
+            if h is None:
+                raise RuntimeError(f"no NVML device with PCI bus id {want}")
             self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM)
             self._stop = threading.Event()
 
