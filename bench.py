@@ -96,14 +96,14 @@ class ClockSampler:
             import torch
 
             pynvml.nvmlInit()
-            # match this CUDA device to its NVML handle by PCI bus id (NVML order may differ)
-            want = str(torch.cuda.get_device_properties(self.cuda_index).pci_bus_id).lower()[-7:]
+            # match this CUDA device to its NVML handle by PCI location (NVML order may differ)
+            props = torch.cuda.get_device_properties(self.cuda_index)
+            want = (int(getattr(props, "pci_domain_id", 0)), int(props.pci_bus_id), int(props.pci_device_id))
             h = None
             for i in range(pynvml.nvmlDeviceGetCount()):
                 cand = pynvml.nvmlDeviceGetHandleByIndex(i)
-                bus = pynvml.nvmlDeviceGetPciInfo(cand).busId
-                bus = bus.decode() if isinstance(bus, bytes) else str(bus)
-                if bus.lower()[-7:] == want:
+                info = pynvml.nvmlDeviceGetPciInfo(cand)
+                if (int(info.domain), int(info.bus), int(info.device)) == want:
                     h = cand
                     break
             if h is None:
