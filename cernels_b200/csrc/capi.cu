@@ -38,6 +38,7 @@ PrefillWorkspace carve_prefill(const cernels_moe_shape& s, void* base, F&& done)
   w.perm_token = c.take<int>(tk + 1);
   w.perm_weight = c.take<float>(tk + 1);
   w.inv = c.take<int>(tk + 1);
+  w.gathered = c.take<__nv_bfloat16>(tk * s.hidden + 8);
   w.glu = c.take<__nv_bfloat16>(tk * s.intermediate + 8);
   w.down_out = c.take<__nv_bfloat16>(tk * s.hidden + 8);
   done(c.off);
@@ -188,15 +189,14 @@ static int run_prefill(const cernels_moe_shape* shape, const void* x, const void
   err = launch_route(indices, weights, s.tokens, s.topk, s.experts, ws, stream);
   if (err != cudaSuccess) return cuda_rc(err);
   mark(1);
-  // The gate/up GEMM gathers its A rows straight from x (tile::gather4 on perm_token); rows at
-  // or past offsets[E] (skipped ids) read token 0 and are never stored.
+  // Rows at or past offsets[E] belong to no expert (skipped ids): not gathered, never read.
+  err = launch_gather(static_cast<const __nv_bfloat16*>(x), ws.perm_token, tk, ws.offsets + s.experts, s.hidden,
+                      ws.gathered, stream);
+  if (err != cudaSuccess) return cuda_rc(err);
   mark(2);
   const int sms = device_sm_count();
   GroupedGemmArgs g1{};
-  g1.a = static_cast<const __nv_bfloat16*>(x);
-  g1.a_rows = ws.perm_token;
-  g1.a_rows_count = ws.offsets + s.experts;
-  g1.a_source_rows = s.tokens;
+  g1.a = ws.gathered;
   g1.b = static_cast<const __nv_bfloat16*>(gate_up_proj);
   g1.bias = gptoss ? gate_up_bias : nullptr;
   g1.out = ws.glu;
@@ -216,7 +216,7 @@ static int run_prefill(const cernels_moe_shape* shape, const void* x, const void
   g2.a = ws.glu;
   g2.b = static_cast<const __nv_bfloat16*>(down_proj);
   g2.bias = gptoss ? down_bias : nullptr;
-  g2.out = ws.down_out;  // (no row gather for the down GEMM)
+  g2.out = ws.down_out;
   g2.offsets = ws.offsets;
   g2.mtile_offsets = ws.mtile_offsets;
   g2.status = ws.status;

@@ -11,9 +11,7 @@
 // (expert e, n-tile, m-tile) through the per-expert tile prefix mtile_offsets, read on
 // the device, so there is no host synchronisation. Each CTA (one per SM) runs:
 //   warp 0      TMA producer: A tile [128 x 64] and B tile [256 x 64] per stage
-//               (128-byte swizzle, 4-stage ring of 48 KB stages). For the gate/up GEMM of
-//               the routed path, A rows are gathered straight from x with tile::gather4
-//               (each lane 4 rows), so no permuted copy of x is materialised.
+//               (128-byte swizzle, 4-stage ring of 48 KB stages)
 //   warp 1      allocates 512 TMEM columns (two 128x256 fp32 accumulators) and issues
 //               tcgen05.mma (M=128, N=256, K=16) from one thread; tcgen05.commit frees
 //               smem stages and publishes finished accumulators
@@ -47,7 +45,6 @@ constexpr float kGptOssLimit = 7.0f;
 constexpr float kGptOssAlpha = 1.702f;
 
 __host__ __device__ constexpr bool mode_is_gptoss(int mode) { return mode == kGateUpGptOss || mode == kDownGptOss; }
-__host__ __device__ constexpr bool mode_is_gate_up(int mode) { return mode == kGateUpLinear || mode == kGateUpGptOss; }
 
 // Number of n-tiles of one expert's output.
 __host__ __device__ inline int n_tiles_for(int mode, int n, int bn) {
@@ -147,43 +144,23 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   if (warp == 0) {
     // ------------------------------------------------------------ TMA producer
-    // Lane 0 owns the ring; with a row gather all 32 lanes issue one gather4 (4 rows) each.
-    const bool gather = mode_is_gate_up(kMode) && args.a_rows != nullptr;
-    const int valid_rows = gather ? *args.a_rows_count : 0;
-    int stage = 0;
-    uint32_t phase = 0;
-    bool ok = true;
-    for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x) {
-      const TileCoord c = decode_tile(t, n_tiles, s_mt, experts);
-      const int row0 = args.offsets[c.expert] + c.m_tile * BM;
-      const int we = c.expert % args.weight_experts;  // weight slab of this row group
-      int src_row[4] = {0, 0, 0, 0};
-      if (gather) {
-#pragma unroll
-        for (int j = 0; j < 4; ++j) {
-          const int r = row0 + 4 * lane + j;
-          src_row[j] = r < valid_rows ? args.a_rows[r] : 0;
-        }
-      }
-      for (int kb = 0; kb < k_blocks; ++kb) {
-        int wait_ok = 1;
-        if (lane == 0)
-          wait_ok = mbar_wait_bounded(&empty_bar[stage], phase ^ 1u, args.status, kStatusTimeoutProducer, abort_flag);
-        if (!__shfl_sync(0xffffffffu, wait_ok, 0)) {
-          ok = false;
-          break;
-        }
-        uint8_t* a_dst = smem_a + stage * kABytes;
-        uint8_t* b_dst = smem_b + stage * kBBytes;
-        if (lane == 0) mbar_arrive_expect_tx(&full_bar[stage], kABytes + kBBytes);
-        __syncwarp();
-        if (gather) {
-          tma_gather4(a_dst + lane * 4 * (BK * 2), &tmap_a, &full_bar[stage], kb * BK, src_row[0], src_row[1],
-                      src_row[2], src_row[3], kCacheEvictNormal);
-        } else if (lane == 0) {
+    if (elect_one()) {
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x) {
+        const TileCoord c = decode_tile(t, n_tiles, s_mt, experts);
+        const int row0 = args.offsets[c.expert] + c.m_tile * BM;
+        const int we = c.expert % args.weight_experts;  // weight slab of this row group
+        for (int kb = 0; kb < k_blocks; ++kb) {
+          if (!mbar_wait_bounded(&empty_bar[stage], phase ^ 1u, args.status, kStatusTimeoutProducer, abort_flag)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&full_bar[stage], kABytes + kBBytes);
+          uint8_t* a_dst = smem_a + stage * kABytes;
+          uint8_t* b_dst = smem_b + stage * kBBytes;
           tma_load_2d(a_dst, &tmap_a, &full_bar[stage], kb * BK, row0, kCacheEvictNormal);
-        }
-        if (lane == 0) {
           if constexpr (kMode == kGateUpLinear) {
             const int f0 = c.n_tile * 128;
             const int half_f = args.n / 2;
@@ -196,13 +173,13 @@ __global__ void __launch_bounds__(kThreads, 1)
             // N-major weights: BN/64 boxes of 64 columns, each [64 K rows x 128 bytes].
 #pragma unroll
             for (int j = 0; j < BN / 64; ++j)
-              tma_load_3d(b_dst + j * kBoxBytes, &tmap_b, &full_bar[stage], c.n_tile * BN + 64 * j, kb * BK, we,
-                          kCacheEvictNormal);
+              tma_load_3d(b_dst + j * kBoxBytes, &tmap_b, &full_bar[stage], c.n_tile * BN + 64 * j, kb * BK,
+                          we, kCacheEvictNormal);
           }
-        }
-        if (++stage == kStages) {
-          stage = 0;
-          phase ^= 1u;
+          if (++stage == kStages) {
+            stage = 0;
+            phase ^= 1u;
+          }
         }
       }
     }
@@ -374,13 +351,7 @@ bool encode_map(CUtensorMap* map, const void* ptr, int rank, const uint64_t* dim
 template <int kMode, int BN>
 cudaError_t launch_mode(const GroupedGemmArgs& args, int num_sms, cudaStream_t stream) {
   CUtensorMap map_a, map_b;
-  if (mode_is_gate_up(kMode) && args.a_rows) {
-    // row-gather map over the un-permuted source: one-row boxes, 64 columns (128 B)
-    const uint64_t dims[2] = {static_cast<uint64_t>(args.k), static_cast<uint64_t>(args.a_source_rows)};
-    const uint64_t strides[1] = {static_cast<uint64_t>(args.k) * 2};
-    const uint32_t box[2] = {BK, 1};
-    if (!encode_map(&map_a, args.a, 2, dims, strides, box)) return cudaErrorInvalidValue;
-  } else {
+  {
     const uint64_t dims[2] = {static_cast<uint64_t>(args.k), static_cast<uint64_t>(args.rows)};
     const uint64_t strides[1] = {static_cast<uint64_t>(args.k) * 2};
     const uint32_t box[2] = {BK, BM};

@@ -35,6 +35,7 @@ struct PrefillWorkspace {
   int* perm_token;      // [Tk] token id of each permuted row
   float* perm_weight;   // [Tk] router weight of each permuted row
   int* inv;             // [Tk] permuted row of each flat entry (-1 when skipped)
+  __nv_bfloat16* gathered;  // [Tk, H] token rows in permuted (expert-major) order
   __nv_bfloat16* glu;       // [Tk, F] activation output of the gate/up GEMM
   __nv_bfloat16* down_out;  // [Tk, H] output of the down GEMM (unweighted)
 };
@@ -79,11 +80,6 @@ struct GroupedGemmArgs {
   int out_cols;                // F for gate/up, H for down
   int weight_experts;          // experts in the weight tensors; row group g uses expert g % weight_experts
   const int* group_rows;       // optional [groups]: rows of group g (default offsets[g+1] - offsets[g])
-  // Optional row gather for A (gate/up GEMM): row i of the A operand is row a_rows[i] of `a`
-  // (a has a_source_rows rows); rows at or past *a_rows_count read row 0 and are discarded.
-  const int* a_rows;
-  const int* a_rows_count;
-  int a_source_rows;
 };
 
 enum GemmMode : int {

@@ -119,19 +119,6 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, u
       : "memory");
 }
 
-// Row gather: 4 rows (arbitrary row coordinates r0..r3) x one 64-column box of a 2-D tensor
-// map whose box is one row high, written as 4 consecutive 128-byte rows at dst (swizzled like
-// a tile load). `col` must be a multiple of 64 elements (16-byte aligned).
-__device__ __forceinline__ void tma_gather4(void* dst, const CUtensorMap* map, uint64_t* bar, int col, int r0, int r1,
-                                            int r2, int r3, uint64_t cache_hint) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.tile::gather4.mbarrier::complete_tx::bytes.L2::cache_hint"
-      " [%0], [%1, {%3, %4, %5, %6, %7}], [%2], %8;" ::"r"(smem_u32(dst)),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(smem_u32(bar)), "r"(col), "r"(r0), "r"(r1), "r"(r2), "r"(r3),
-      "l"(cache_hint)
-      : "memory");
-}
-
 // L2 eviction-priority hints (createpolicy encodings).
 constexpr uint64_t kCacheEvictNormal = 0x1000000000000000ull;
 constexpr uint64_t kCacheEvictFirst = 0x12F0000000000000ull;
