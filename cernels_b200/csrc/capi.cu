@@ -166,14 +166,28 @@ static int validate_common(const cernels_moe_shape* shape, const void* x, const 
 
 // Launch sequence of the prefill path. When `events` is non-null, events[i] is recorded
 // before stage i and events[5] after the last stage.
+// With shared_w1 / shared_w2 (one always-on expert, same F), `shape` describes the routed
+// experts and top-k; indices / weights carry topk + 1 columns, the last one routing every
+// token to expert id E (the shared expert) with its gate weight.
 static int run_prefill(const cernels_moe_shape* shape, const void* x, const void* gate_up_proj,
                        const float* gate_up_bias, const void* down_proj, const float* down_bias,
                        const int32_t* indices, const float* weights, void* out, void* workspace,
-                       size_t workspace_bytes, cudaStream_t stream, cudaEvent_t* events) {
+                       size_t workspace_bytes, cudaStream_t stream, cudaEvent_t* events,
+                       const void* shared_w1 = nullptr, const void* shared_w2 = nullptr) {
   const int rc0 = check_shape(shape);
   if (rc0) return rc0;
-  const cernels_moe_shape s = *shape;
-  int rc = validate_common(shape, x, gate_up_proj, down_proj, indices, weights, out, workspace, workspace_bytes,
+  const bool has_shared = shared_w1 != nullptr;
+  const int routed_experts = shape->experts;
+  cernels_moe_shape s = *shape;
+  if (has_shared) {
+    if (!shared_w2) return CERNELS_E_NULL;
+    if (s.layout != CERNELS_LAYOUT_LINEAR) return CERNELS_E_UNSUPPORTED;
+    if (!aligned16(shared_w1) || !aligned16(shared_w2)) return CERNELS_E_ALIGNMENT;
+    s.experts += 1;  // expert id E is the shared expert
+    s.topk += 1;     // its slot is the last column
+    if (check_shape(&s)) return check_shape(&s);
+  }
+  int rc = validate_common(&s, x, gate_up_proj, down_proj, indices, weights, out, workspace, workspace_bytes,
                            prefill_workspace_bytes(s));
   if (rc || s.tokens == 0) return rc;
   const PrefillWorkspace ws = carve_prefill_workspace(s, workspace);
@@ -208,7 +222,11 @@ static int run_prefill(const cernels_moe_shape* shape, const void* x, const void
   g1.k = s.hidden;
   g1.n = 2 * s.intermediate;
   g1.out_cols = s.intermediate;
-  g1.weight_experts = s.experts;
+  g1.weight_experts = routed_experts;
+  if (has_shared) {
+    g1.b_extra = static_cast<const __nv_bfloat16*>(shared_w1);
+    g1.extra_group = routed_experts;
+  }
   err = launch_grouped_gemm(gptoss ? kGateUpGptOss : kGateUpLinear, g1, sms, stream);
   if (err != cudaSuccess) return cuda_rc(err);
   mark(3);
@@ -225,7 +243,11 @@ static int run_prefill(const cernels_moe_shape* shape, const void* x, const void
   g2.k = s.intermediate;
   g2.n = s.hidden;
   g2.out_cols = s.hidden;
-  g2.weight_experts = s.experts;
+  g2.weight_experts = routed_experts;
+  if (has_shared) {
+    g2.b_extra = static_cast<const __nv_bfloat16*>(shared_w2);
+    g2.extra_group = routed_experts;
+  }
   err = launch_grouped_gemm(gptoss ? kDownGptOss : kDownLinear, g2, sms, stream);
   if (err != cudaSuccess) return cuda_rc(err);
   mark(4);
@@ -241,6 +263,16 @@ int cernels_moe_experts(const cernels_moe_shape* shape, const void* x, const voi
                         size_t workspace_bytes, void* stream) {
   return run_prefill(shape, x, gate_up_proj, gate_up_bias, down_proj, down_bias, indices, weights, out, workspace,
                      workspace_bytes, static_cast<cudaStream_t>(stream), nullptr);
+}
+
+int cernels_moe_experts_shared(const cernels_moe_shape* shape, const void* x, const void* gate_up_proj,
+                               const void* down_proj, const void* shared_gate_up_proj, const void* shared_down_proj,
+                               const int32_t* indices, const float* weights, void* out, void* workspace,
+                               size_t workspace_bytes, void* stream) {
+  if (!shared_gate_up_proj || !shared_down_proj) return CERNELS_E_NULL;
+  return run_prefill(shape, x, gate_up_proj, nullptr, down_proj, nullptr, indices, weights, out, workspace,
+                     workspace_bytes, static_cast<cudaStream_t>(stream), nullptr, shared_gate_up_proj,
+                     shared_down_proj);
 }
 
 int cernels_moe_experts_profiled(const cernels_moe_shape* shape, const void* x, const void* gate_up_proj,
@@ -346,14 +378,15 @@ int cernels_moe_grouped_experts(const cernels_moe_shape* shape, int32_t groups, 
 }
 
 int cernels_router_topk(const void* logits, int32_t logits_bf16, int32_t tokens, int32_t experts, int32_t topk,
-                        int32_t mode, int32_t renorm, int32_t* indices, float* weights, void* stream) {
+                        int32_t mode, int32_t renorm, int32_t shared_gate, int32_t* indices, float* weights,
+                        void* stream) {
   if (tokens < 0 || experts <= 0 || experts > 1024 || topk <= 0 || topk > 32 || topk > experts)
     return CERNELS_E_INVALID_SHAPE;
   if (mode != CERNELS_ROUTER_TOPK_SOFTMAX && mode != CERNELS_ROUTER_SOFTMAX_TOPK) return CERNELS_E_INVALID_SHAPE;
   if (tokens == 0) return CERNELS_OK;
   if (!logits || !indices || !weights) return CERNELS_E_NULL;
-  return cuda_rc(launch_router_topk(logits, logits_bf16 != 0, tokens, experts, topk, mode, renorm != 0, indices,
-                                    weights, static_cast<cudaStream_t>(stream)));
+  return cuda_rc(launch_router_topk(logits, logits_bf16 != 0, tokens, experts, topk, mode, renorm != 0,
+                                    shared_gate != 0, indices, weights, static_cast<cudaStream_t>(stream)));
 }
 
 int cernels_moe_route(const cernels_moe_shape* shape, const int32_t* indices, const float* weights,

@@ -93,7 +93,7 @@ __device__ __forceinline__ float gptoss_glu(float gate, float up) {
 template <int kMode, int BN>
 __global__ void __launch_bounds__(kThreads, 1)
     grouped_gemm_kernel(const __grid_constant__ CUtensorMap tmap_a, const __grid_constant__ CUtensorMap tmap_b,
-                        GroupedGemmArgs args) {
+                        const __grid_constant__ CUtensorMap tmap_b_extra, GroupedGemmArgs args) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* smem_a = smem;
@@ -131,6 +131,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     fence_barrier_init();
     tma_prefetch_desc(&tmap_a);
     tma_prefetch_desc(&tmap_b);
+    if (args.b_extra != nullptr) tma_prefetch_desc(&tmap_b_extra);
   }
   if (warp == 1) {
     tmem_alloc(tmem_base_slot, kTmemCols);
@@ -151,7 +152,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x) {
         const TileCoord c = decode_tile(t, n_tiles, s_mt, experts);
         const int row0 = args.offsets[c.expert] + c.m_tile * BM;
-        const int we = c.expert % args.weight_experts;  // weight slab of this row group
+        const bool extra = args.b_extra != nullptr && c.expert == args.extra_group;
+        const CUtensorMap* bmap = extra ? &tmap_b_extra : &tmap_b;
+        const int we = extra ? 0 : c.expert % args.weight_experts;  // weight slab of this row group
         for (int kb = 0; kb < k_blocks; ++kb) {
           if (!mbar_wait_bounded(&empty_bar[stage], phase ^ 1u, args.status, kStatusTimeoutProducer, abort_flag)) {
             ok = false;
@@ -164,16 +167,16 @@ __global__ void __launch_bounds__(kThreads, 1)
           if constexpr (kMode == kGateUpLinear) {
             const int f0 = c.n_tile * 128;
             const int half_f = args.n / 2;
-            tma_load_3d(b_dst, &tmap_b, &full_bar[stage], kb * BK, f0, we, kCacheEvictNormal);
-            tma_load_3d(b_dst + kBBytes / 2, &tmap_b, &full_bar[stage], kb * BK, half_f + f0, we,
+            tma_load_3d(b_dst, bmap, &full_bar[stage], kb * BK, f0, we, kCacheEvictNormal);
+            tma_load_3d(b_dst + kBBytes / 2, bmap, &full_bar[stage], kb * BK, half_f + f0, we,
                         kCacheEvictNormal);
           } else if constexpr (kMode == kDownLinear) {
-            tma_load_3d(b_dst, &tmap_b, &full_bar[stage], kb * BK, c.n_tile * BN, we, kCacheEvictNormal);
+            tma_load_3d(b_dst, bmap, &full_bar[stage], kb * BK, c.n_tile * BN, we, kCacheEvictNormal);
           } else {
             // N-major weights: BN/64 boxes of 64 columns, each [64 K rows x 128 bytes].
 #pragma unroll
             for (int j = 0; j < BN / 64; ++j)
-              tma_load_3d(b_dst + j * kBoxBytes, &tmap_b, &full_bar[stage], c.n_tile * BN + 64 * j, kb * BK,
+              tma_load_3d(b_dst + j * kBoxBytes, bmap, &full_bar[stage], c.n_tile * BN + 64 * j, kb * BK,
                           we, kCacheEvictNormal);
           }
           if (++stage == kStages) {
@@ -235,7 +238,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (!mbar_wait_bounded(&tfull_bar[acc], acc_phase, args.status, kStatusTimeoutEpilogue, abort_flag)) break;
       tc_fence_after();
       const TileCoord c = decode_tile(t, n_tiles, s_mt, experts);
-      const int e = c.expert % args.weight_experts;  // weight slab (bias row) of this row group
+      const int e = (args.b_extra != nullptr && c.expert == args.extra_group) ? 0 : c.expert % args.weight_experts;
       const int row_begin = args.offsets[c.expert];
       const int rows_e = args.group_rows ? args.group_rows[c.expert] : args.offsets[c.expert + 1] - row_begin;
       const int local_row = c.m_tile * BM + quarter * 32 + lane;
@@ -357,19 +360,27 @@ cudaError_t launch_mode(const GroupedGemmArgs& args, int num_sms, cudaStream_t s
     const uint32_t box[2] = {BK, BM};
     if (!encode_map(&map_a, args.a, 2, dims, strides, box)) return cudaErrorInvalidValue;
   }
-  const uint64_t E = static_cast<uint64_t>(args.weight_experts);
-  if constexpr (kMode == kGateUpLinear || kMode == kDownLinear) {
-    // Weight [E, N, K] (K contiguous): dims (K, N, E).
-    const uint64_t dims[3] = {static_cast<uint64_t>(args.k), static_cast<uint64_t>(args.n), E};
-    const uint64_t strides[2] = {static_cast<uint64_t>(args.k) * 2, static_cast<uint64_t>(args.k) * args.n * 2};
-    const uint32_t box[3] = {BK, kMode == kGateUpLinear ? 128u : static_cast<uint32_t>(BN), 1};
-    if (!encode_map(&map_b, args.b, 3, dims, strides, box)) return cudaErrorInvalidValue;
+  auto encode_b = [&](CUtensorMap* map, const __nv_bfloat16* ptr, uint64_t E) -> bool {
+    if constexpr (kMode == kGateUpLinear || kMode == kDownLinear) {
+      // Weight [E, N, K] (K contiguous): dims (K, N, E).
+      const uint64_t dims[3] = {static_cast<uint64_t>(args.k), static_cast<uint64_t>(args.n), E};
+      const uint64_t strides[2] = {static_cast<uint64_t>(args.k) * 2, static_cast<uint64_t>(args.k) * args.n * 2};
+      const uint32_t box[3] = {BK, kMode == kGateUpLinear ? 128u : static_cast<uint32_t>(BN), 1};
+      return encode_map(map, ptr, 3, dims, strides, box);
+    } else {
+      // Weight [E, K, N] (N contiguous): dims (N, K, E), 64-column boxes.
+      const uint64_t dims[3] = {static_cast<uint64_t>(args.n), static_cast<uint64_t>(args.k), E};
+      const uint64_t strides[2] = {static_cast<uint64_t>(args.n) * 2, static_cast<uint64_t>(args.k) * args.n * 2};
+      const uint32_t box[3] = {64, BK, 1};
+      return encode_map(map, ptr, 3, dims, strides, box);
+    }
+  };
+  CUtensorMap map_b_extra;
+  if (!encode_b(&map_b, args.b, static_cast<uint64_t>(args.weight_experts))) return cudaErrorInvalidValue;
+  if (args.b_extra != nullptr) {
+    if (!encode_b(&map_b_extra, args.b_extra, 1)) return cudaErrorInvalidValue;
   } else {
-    // Weight [E, K, N] (N contiguous): dims (N, K, E), 64-column boxes.
-    const uint64_t dims[3] = {static_cast<uint64_t>(args.n), static_cast<uint64_t>(args.k), E};
-    const uint64_t strides[2] = {static_cast<uint64_t>(args.n) * 2, static_cast<uint64_t>(args.k) * args.n * 2};
-    const uint32_t box[3] = {64, BK, 1};
-    if (!encode_map(&map_b, args.b, 3, dims, strides, box)) return cudaErrorInvalidValue;
+    map_b_extra = map_b;
   }
   const size_t smem = smem_fixed(BN) + 1024 + static_cast<size_t>(args.experts + 1) * sizeof(int);
   static bool attr_set = false;
@@ -385,7 +396,7 @@ cudaError_t launch_mode(const GroupedGemmArgs& args, int num_sms, cudaStream_t s
   const long long max_tiles = max_mtiles * n_tiles;
   const int grid = static_cast<int>(max_tiles < num_sms ? max_tiles : num_sms);
   if (grid <= 0) return cudaSuccess;
-  grouped_gemm_kernel<kMode, BN><<<grid, kThreads, smem, stream>>>(map_a, map_b, args);
+  grouped_gemm_kernel<kMode, BN><<<grid, kThreads, smem, stream>>>(map_a, map_b, map_b_extra, args);
   return cudaGetLastError();
 }
 

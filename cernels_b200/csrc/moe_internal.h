@@ -80,6 +80,10 @@ struct GroupedGemmArgs {
   int out_cols;                // F for gate/up, H for down
   int weight_experts;          // experts in the weight tensors; row group g uses expert g % weight_experts
   const int* group_rows;       // optional [groups]: rows of group g (default offsets[g+1] - offsets[g])
+  // Optional always-on extra group (a shared expert): group `extra_group` takes its weights
+  // from b_extra (one slab, same layout as b) instead of b. Unused when b_extra is null.
+  const __nv_bfloat16* b_extra;
+  int extra_group;
 };
 
 enum GemmMode : int {
@@ -107,7 +111,7 @@ cudaError_t launch_decode(const DecodeArgs& a, const DecodeWorkspace& ws, cudaSt
 // Router tail (router.cu). mode 0: top-k of the logits, softmax over the k values rounded to
 // bf16; mode 1: softmax over all experts (fp32), top-k, optional renormalisation.
 cudaError_t launch_router_topk(const void* logits, int bf16, int tokens, int experts, int topk, int mode, int renorm,
-                               int32_t* idx, float* w, cudaStream_t stream);
+                               int shared_gate, int32_t* idx, float* w, cudaStream_t stream);
 
 int device_sm_count();
 

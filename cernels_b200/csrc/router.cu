@@ -29,12 +29,15 @@ __device__ __forceinline__ float to_f32<__nv_bfloat16>(__nv_bfloat16 v) { return
 template <typename T, int kPerLane>
 __global__ void __launch_bounds__(kRouterWarps * 32) router_topk_kernel(const T* __restrict__ logits, int tokens,
                                                                         int experts, int topk, int mode, int renorm,
+                                                                        int shared_gate,
                                                                         int32_t* __restrict__ indices,
                                                                         float* __restrict__ weights) {
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int t = blockIdx.x * kRouterWarps + warp;
   if (t >= tokens) return;
-  const T* row = logits + static_cast<size_t>(t) * experts;
+  // With a shared-gate column, logits rows hold experts + 1 values (the last is the gate).
+  const T* row = logits + static_cast<size_t>(t) * (experts + shared_gate);
+  const int out_stride = topk + shared_gate;
   float v[kPerLane];
 #pragma unroll
   for (int j = 0; j < kPerLane; ++j) {
@@ -104,33 +107,39 @@ __global__ void __launch_bounds__(kRouterWarps * 32) router_topk_kernel(const T*
     w = p;
   }
   if (lane < topk) {
-    indices[static_cast<size_t>(t) * topk + lane] = sel_e;
-    weights[static_cast<size_t>(t) * topk + lane] = w;
+    indices[static_cast<size_t>(t) * out_stride + lane] = sel_e;
+    weights[static_cast<size_t>(t) * out_stride + lane] = w;
+  }
+  if (shared_gate && lane == 0) {  // always-on shared expert: id `experts`, weight sigmoid(gate)
+    const float gl = to_f32(row[experts]);
+    indices[static_cast<size_t>(t) * out_stride + topk] = experts;
+    weights[static_cast<size_t>(t) * out_stride + topk] = 1.0f / (1.0f + __expf(-gl));
   }
 }
 
 template <typename T>
-cudaError_t launch_t(const void* logits, int tokens, int experts, int topk, int mode, int renorm, int32_t* idx,
-                     float* w, cudaStream_t stream) {
+cudaError_t launch_t(const void* logits, int tokens, int experts, int topk, int mode, int renorm, int shared,
+                     int32_t* idx, float* w, cudaStream_t stream) {
   const int blocks = (tokens + kRouterWarps - 1) / kRouterWarps;
   const T* l = static_cast<const T*>(logits);
   if (experts <= 64)
-    router_topk_kernel<T, 2><<<blocks, kRouterWarps * 32, 0, stream>>>(l, tokens, experts, topk, mode, renorm, idx, w);
+    router_topk_kernel<T, 2><<<blocks, kRouterWarps * 32, 0, stream>>>(l, tokens, experts, topk, mode, renorm, shared, idx, w);
   else if (experts <= 256)
-    router_topk_kernel<T, 8><<<blocks, kRouterWarps * 32, 0, stream>>>(l, tokens, experts, topk, mode, renorm, idx, w);
+    router_topk_kernel<T, 8><<<blocks, kRouterWarps * 32, 0, stream>>>(l, tokens, experts, topk, mode, renorm, shared, idx, w);
   else
     router_topk_kernel<T, kMaxPerLane><<<blocks, kRouterWarps * 32, 0, stream>>>(l, tokens, experts, topk, mode,
-                                                                                 renorm, idx, w);
+                                                                                 renorm, shared, idx, w);
   return cudaGetLastError();
 }
 
 }  // namespace
 
 cudaError_t launch_router_topk(const void* logits, int bf16, int tokens, int experts, int topk, int mode, int renorm,
-                               int32_t* idx, float* w, cudaStream_t stream) {
+                               int shared_gate, int32_t* idx, float* w, cudaStream_t stream) {
   if (tokens <= 0) return cudaSuccess;
-  return bf16 ? launch_t<__nv_bfloat16>(logits, tokens, experts, topk, mode, renorm, idx, w, stream)
-              : launch_t<float>(logits, tokens, experts, topk, mode, renorm, idx, w, stream);
+  const int sg = shared_gate ? 1 : 0;
+  return bf16 ? launch_t<__nv_bfloat16>(logits, tokens, experts, topk, mode, renorm, sg, idx, w, stream)
+              : launch_t<float>(logits, tokens, experts, topk, mode, renorm, sg, idx, w, stream);
 }
 
 }  // namespace cernels

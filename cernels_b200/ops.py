@@ -204,6 +204,36 @@ def gpt_oss_moe_experts_decode(x, gate_up_proj, gate_up_bias, down_proj, down_bi
     return ops.gpt_oss_moe_experts_decode(x, gate_up_proj, gate_up_bias, down_proj, down_bias, indices, weights, topk)
 
 
+def run_experts_shared(x, gate_up_proj, down_proj, shared_gate_up, shared_down, indices, weights, topk):
+    """Routed experts (LINEAR layout) + one always-on shared expert in the same launches.
+    indices / weights: [T, topk + 1], last column = (E, shared gate weight)."""
+    for name, t in (("x", x), ("gate_up_proj", gate_up_proj), ("down_proj", down_proj), ("indices", indices),
+                    ("weights", weights), ("shared_gate_up", shared_gate_up), ("shared_down", shared_down)):
+        _check(t.is_cuda and t.device == x.device and t.is_contiguous(), f"{name} must be a contiguous CUDA tensor on x's device")
+    _check(x.dtype == torch.bfloat16 and x.dim() == 2, "x must be [T, H] bf16")
+    _check(indices.dtype == torch.int32 and weights.dtype == torch.float32, "indices int32, weights fp32")
+    _check(tuple(indices.shape) == (x.shape[0], topk + 1) and tuple(weights.shape) == (x.shape[0], topk + 1),
+           "indices / weights must be [T, topk + 1]")
+    E, F = gate_up_proj.shape[0], gate_up_proj.shape[1] // 2
+    _check(tuple(shared_gate_up.shape) == (1, 2 * F, x.shape[1]) and tuple(shared_down.shape) == (1, x.shape[1], F),
+           "shared expert weights must be [1, 2F, H] and [1, H, F]")
+    out = torch.empty_like(x)
+    if x.shape[0] == 0:
+        return out
+    shape = shape_of(x, gate_up_proj, down_proj, topk, _lib.LAYOUT_LINEAR)
+    ws_shape = _lib.MoeShape(shape.tokens, shape.hidden, shape.experts + 1, shape.intermediate, shape.topk + 1,
+                             shape.layout)
+    ws_bytes = _lib.workspace_bytes(ws_shape, False)
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=x.device)
+    with torch.cuda.device(x.device):
+        rc = _lib.load().cernels_moe_experts_shared(
+            ctypes.byref(shape), x.data_ptr(), gate_up_proj.data_ptr(), down_proj.data_ptr(), shared_gate_up.data_ptr(),
+            shared_down.data_ptr(), indices.data_ptr(), weights.data_ptr(), out.data_ptr(), ws.data_ptr(), ws_bytes,
+            _stream_handle(x.device))
+    _lib.check(rc, "cernels_moe_experts_shared")
+    return out
+
+
 # ---------------------------------------------------------------- stage entry points
 def route(indices: torch.Tensor, weights: torch.Tensor, experts: int):
     """Routing only: returns (offsets [E+1], perm_token [Tk], perm_weight [Tk], inv [Tk]).
@@ -262,19 +292,22 @@ ROUTER_TOPK_SOFTMAX = 0
 ROUTER_SOFTMAX_TOPK = 1
 
 
-def router_topk(logits: torch.Tensor, topk: int, mode: int, renorm: bool = False):
+def router_topk(logits: torch.Tensor, topk: int, mode: int, renorm: bool = False, shared_gate: bool = False):
     """Top-k expert ids (int32) and fp32 routing weights from router logits [T, E] in one launch
-    (see cernels_router_topk in include/cernels_b200.h)."""
+    (see cernels_router_topk in include/cernels_b200.h). With shared_gate the last logits column
+    is a shared expert's gate: outputs get a (E, sigmoid(gate)) slot appended."""
     _check(logits.is_cuda and logits.dim() == 2 and logits.dtype in (torch.bfloat16, torch.float32),
            "logits must be a [T, E] bf16 or fp32 CUDA tensor")
     logits = logits.contiguous()
     T, E = logits.shape
-    idx = torch.empty(T, topk, dtype=torch.int32, device=logits.device)
-    w = torch.empty(T, topk, dtype=torch.float32, device=logits.device)
+    E -= int(bool(shared_gate))
+    cols = topk + int(bool(shared_gate))
+    idx = torch.empty(T, cols, dtype=torch.int32, device=logits.device)
+    w = torch.empty(T, cols, dtype=torch.float32, device=logits.device)
     with torch.cuda.device(logits.device):
         rc = _lib.load().cernels_router_topk(logits.data_ptr(), int(logits.dtype == torch.bfloat16), T, E, int(topk),
-                                             int(mode), int(bool(renorm)), idx.data_ptr(), w.data_ptr(),
-                                             _stream_handle(logits.device))
+                                             int(mode), int(bool(renorm)), int(bool(shared_gate)), idx.data_ptr(),
+                                             w.data_ptr(), _stream_handle(logits.device))
     _lib.check(rc, "cernels_router_topk")
     return idx, w
 

@@ -6,7 +6,11 @@ its linear in cuBLAS (torch), softmax + top-k + renorm in one kernel (cernels_ro
 the CUDA op; the always-on shared expert ``sigmoid(shared_expert_gate(x)) *
 shared_expert(x)`` runs through the same CUDA grouped-GEMM path as a one-expert,
 one-slot problem whose router weight is the sigmoid gate (its gate/up weights are
-concatenated once into the [1, 2Fs, H] layout and cached on the block).
+concatenated once into the [1, 2Fs, H] layout and cached on the block). When the shared
+intermediate size equals the routed one (Qwen3-Next: 512), ``kernel`` instead folds the shared
+expert into the routed call: one router GEMM over [W_router; g_shared], one router-tail kernel
+that appends a (E, sigmoid(gate)) slot to every token, and the shared expert as an always-on
+group of the same grouped GEMMs (cernels_moe_experts_shared).
 """
 
 import torch
@@ -45,17 +49,40 @@ def route(xf, block):
     return ops.router_topk(logits, int(block.gate.top_k), ops.ROUTER_SOFTMAX_TOPK, bool(block.gate.norm_topk_prob))
 
 
+def _router_and_gate(block):
+    """[E + 1, H]: router weight with the shared-expert gate row appended (cached)."""
+    g, sg = block.gate.weight, block.shared_expert_gate.weight
+    stamp = (g.data_ptr(), g._version, sg.data_ptr(), sg._version)
+    return module_cache(block, "router_gate", stamp, lambda: torch.cat([g.data, sg.data], dim=0).contiguous())
+
+
+def fused_shared_supported(block) -> bool:
+    se = block.shared_expert
+    return se.gate_proj.weight.shape[0] == block.experts.gate_up_proj.shape[1] // 2
+
+
 def kernel(x, block):
     if block is None:
         raise RuntimeError("block module not available (meta device)")
     bsz, seqlen, hidden = x.shape
     xf = x.reshape(-1, hidden).contiguous()
     with torch.no_grad():
-        idx, w = route(xf, block)
         e = block.experts
-        routed = ops.qwen3_next_moe_experts(xf, e.gate_up_proj.data.contiguous(), e.down_proj.data.contiguous(),
-                                            idx, w, int(block.gate.top_k))
-        out = routed + shared_expert(xf, block)
+        k = int(block.gate.top_k)
+        if fused_shared_supported(block):
+            # router + shared gate in one GEMM, top-k + renorm + sigmoid gate in one kernel, and
+            # the shared expert as an always-on group of the same grouped GEMMs
+            logits = torch.nn.functional.linear(xf, _router_and_gate(block))
+            idx, w = ops.router_topk(logits, k, ops.ROUTER_SOFTMAX_TOPK, bool(block.gate.norm_topk_prob),
+                                     shared_gate=True)
+            sw1, sw2 = _shared_weights(block)
+            out = ops.run_experts_shared(xf, e.gate_up_proj.data.contiguous(), e.down_proj.data.contiguous(), sw1,
+                                         sw2, idx, w, k)
+        else:
+            idx, w = route(xf, block)
+            routed = ops.qwen3_next_moe_experts(xf, e.gate_up_proj.data.contiguous(), e.down_proj.data.contiguous(),
+                                                idx, w, k)
+            out = routed + shared_expert(xf, block)
     return out.reshape(bsz, seqlen, hidden)
 
 

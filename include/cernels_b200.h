@@ -76,6 +76,18 @@ int cernels_moe_experts(const cernels_moe_shape* shape, const void* x, const voi
                         const int32_t* indices, const float* weights, void* out, void* workspace,
                         size_t workspace_bytes, void* stream);
 
+/* Routed experts plus one always-on shared expert in the same launches (LINEAR layout, shared
+ * intermediate size = F): the shared expert is expert id E, every token routes to it in the last
+ * of topk + 1 slots with its gate weight (cernels_router_topk with shared_gate produces that).
+ * shape describes the routed experts (experts = E, topk = k); indices / weights are [T, k + 1];
+ * shared_gate_up_proj [1, 2F, H], shared_down_proj [1, H, F]; workspace =
+ * cernels_moe_workspace_bytes of the shape with experts + 1 and topk + 1. Replaces the routed op
+ * plus the torch shared MLP, sigmoid gate and add of src/kops/registry/qwen3_next_moe_experts.py:31-44. */
+int cernels_moe_experts_shared(const cernels_moe_shape* shape, const void* x, const void* gate_up_proj,
+                               const void* down_proj, const void* shared_gate_up_proj, const void* shared_down_proj,
+                               const int32_t* indices, const float* weights, void* out, void* workspace,
+                               size_t workspace_bytes, void* stream);
+
 /* Decode path (T * topk <= 1024): fused gather-GEMV that streams each selected expert's
  * weights once, deduplicated across tokens. Replaces `cohere2_moe_experts_decode`
  * (src/kops/cohere2_moe_experts/csrc/cohere2_moe_experts.cu:199) and
@@ -123,7 +135,11 @@ int cernels_moe_grouped_experts(const cernels_moe_shape* shape, int32_t groups, 
 #define CERNELS_ROUTER_TOPK_SOFTMAX 0
 #define CERNELS_ROUTER_SOFTMAX_TOPK 1
 int cernels_router_topk(const void* logits, int32_t logits_bf16, int32_t tokens, int32_t experts, int32_t topk,
-                        int32_t mode, int32_t renorm, int32_t* indices, float* weights, void* stream);
+                        int32_t mode, int32_t renorm, int32_t shared_gate, int32_t* indices, float* weights,
+                        void* stream);
+/* shared_gate != 0: logits rows hold E + 1 values, the last being a shared expert's gate logit;
+ * indices / weights get topk + 1 columns, the last = (E, sigmoid(gate logit)) — the input of
+ * cernels_moe_experts_shared. */
 
 /* Gather: rows_out[i, :] = x[perm_token[i], :] for i < rows ([rows, H] bf16). Replaces
  * gather_kernel (src/kops/cohere2_moe_experts/csrc/cohere2_moe_experts.cu:58-65). Used by

@@ -362,3 +362,21 @@ def test_host_pipeline_matches_direct_call():
     HostPipeline().run(step, [x.pin_memory(), idx.pin_memory(), w.pin_memory()], out, chunks=3)
     torch.cuda.synchronize()
     assert torch.equal(out, direct)
+
+
+def test_shared_expert_fused_path_matches_separate_path():
+    """cernels_moe_experts_shared (shared expert as an always-on group) vs the routed op plus
+    the shared expert run as its own one-expert problem."""
+    from cernels_b200.hf_modules import build_module
+    from cernels_b200.registry import qwen3_next_moe_experts as qn
+    cfg = CONFIGS["qwen3_next"].scaled(tokens=300, experts=64, hidden=512, inter=256, shared_inter=256)
+    case = make_case(cfg, device=DEV)
+    _, blk = build_module(case)
+    xf = case.x
+    assert qn.fused_shared_supported(blk)
+    fused = qn.kernel(xf.unsqueeze(0), blk).squeeze(0)
+    idx, w = qn.route(xf, blk)
+    e = blk.experts
+    sep = ops.qwen3_next_moe_experts(xf, e.gate_up_proj.data, e.down_proj.data, idx, w, 10) + qn.shared_expert(xf, blk)
+    ref = sep.float().cpu().numpy()
+    assert_close(fused, ref)
