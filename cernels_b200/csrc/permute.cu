@@ -119,6 +119,8 @@ cudaError_t launch_combine(const __nv_bfloat16* down_out, const int* inv, const 
     combine_kernel<4><<<blocks, kRowThreads, 0, stream>>>(rows, inv, weights, tokens, topk, vec, o);
   } else if (topk <= 8) {
     combine_kernel<8><<<blocks, kRowThreads, 0, stream>>>(rows, inv, weights, tokens, topk, vec, o);
+  } else if (topk <= 12) {
+    combine_kernel<12><<<blocks, kRowThreads, 0, stream>>>(rows, inv, weights, tokens, topk, vec, o);
   } else if (topk <= 16) {
     combine_kernel<16><<<blocks, kRowThreads, 0, stream>>>(rows, inv, weights, tokens, topk, vec, o);
   } else {

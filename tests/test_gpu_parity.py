@@ -374,9 +374,11 @@ def test_shared_expert_fused_path_matches_separate_path():
     _, blk = build_module(case)
     xf = case.x
     assert qn.fused_shared_supported(blk)
-    fused = qn.kernel(xf.unsqueeze(0), blk).squeeze(0)
-    idx, w = qn.route(xf, blk)
-    e = blk.experts
-    sep = ops.qwen3_next_moe_experts(xf, e.gate_up_proj.data, e.down_proj.data, idx, w, 10) + qn.shared_expert(xf, blk)
+    with torch.no_grad():
+        fused = qn.kernel(xf.unsqueeze(0), blk).squeeze(0)
+        idx, w = qn.route(xf, blk)
+        e = blk.experts
+        sep = (ops.qwen3_next_moe_experts(xf, e.gate_up_proj.data, e.down_proj.data, idx, w, 10)
+               + qn.shared_expert(xf, blk))
     ref = sep.float().cpu().numpy()
     assert_close(fused, ref)
