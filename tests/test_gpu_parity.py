@@ -365,20 +365,25 @@ def test_host_pipeline_matches_direct_call():
 
 
 def test_shared_expert_fused_path_matches_separate_path():
-    """cernels_moe_experts_shared (shared expert as an always-on group) vs the routed op plus
-    the shared expert run as its own one-expert problem."""
+    """cernels_moe_experts_shared (shared expert as an always-on group) vs the routed op plus the
+    shared expert run as its own one-expert problem, on the same routing (fused router output)."""
     from cernels_b200.hf_modules import build_module
     from cernels_b200.registry import qwen3_next_moe_experts as qn
     cfg = CONFIGS["qwen3_next"].scaled(tokens=300, experts=64, hidden=512, inter=256, shared_inter=256)
     case = make_case(cfg, device=DEV)
     _, blk = build_module(case)
     xf = case.x
+    k = cfg.topk
     assert qn.fused_shared_supported(blk)
     with torch.no_grad():
-        fused = qn.kernel(xf.unsqueeze(0), blk).squeeze(0)
-        idx, w = qn.route(xf, blk)
+        logits = torch.nn.functional.linear(xf, qn._router_and_gate(blk))
+        idx, w = ops.router_topk(logits, k, ops.ROUTER_SOFTMAX_TOPK, True, shared_gate=True)
+        assert torch.all(idx[:, k] == cfg.experts)
+        sw1, sw2 = qn._shared_weights(blk)
         e = blk.experts
-        sep = (ops.qwen3_next_moe_experts(xf, e.gate_up_proj.data, e.down_proj.data, idx, w, 10)
-               + qn.shared_expert(xf, blk))
-    ref = sep.float().cpu().numpy()
+        fused = ops.run_experts_shared(xf, e.gate_up_proj.data, e.down_proj.data, sw1, sw2, idx, w, k)
+        routed = ops.qwen3_next_moe_experts(xf, e.gate_up_proj.data, e.down_proj.data, idx[:, :k].contiguous(),
+                                            w[:, :k].contiguous(), k)
+        shared = ops.qwen3_next_moe_experts(xf, sw1, sw2, torch.zeros_like(idx[:, :1]), w[:, k:].contiguous(), 1)
+        ref = (routed.float() + shared.float()).cpu().numpy()
     assert_close(fused, ref)
