@@ -173,10 +173,12 @@ def make_step(cfg, case, kind, module, world, rank):
         shard = ep.token_shard(cfg.tokens, rank, world)
         x = case.x[shard].contiguous()
         return (lambda xx: planner.forward(xx)), [x], planner.launches_per_step
+    # launches of this library's kernels per step (router tail 1 + route 3 + gather 1 + 2 GEMMs
+    # + combine 1); the router GEMM runs in cuBLAS through torch
     if kind == "gpt_oss":
-        return (lambda xx: go.kernel(xx.unsqueeze(0), module).squeeze(0)), [case.x], 7
+        return (lambda xx: go.kernel(xx.unsqueeze(0), module).squeeze(0)), [case.x], 8
     if kind == "qwen3_next":
-        return (lambda xx: qn.kernel(xx.unsqueeze(0), module).squeeze(0)), [case.x], 14
+        return (lambda xx: qn.kernel(xx.unsqueeze(0), module).squeeze(0)), [case.x], 8
     idx, w = case.indices, case.weights.to(torch.bfloat16)
     fn = c2.decode_kernel if decode else c2.kernel
     return (lambda xx, ii, ww: fn(xx, ii, ww, module)), [case.x, idx, w], (2 if decode else 7)
