@@ -13,6 +13,8 @@ that appends a (E, sigmoid(gate)) slot to every token, and the shared expert as 
 group of the same grouped GEMMs (cernels_moe_experts_shared).
 """
 
+import os
+
 import torch
 
 from .. import ops
@@ -56,9 +58,12 @@ def _router_and_gate(block):
     return module_cache(block, "router_gate", stamp, lambda: torch.cat([g.data, sg.data], dim=0).contiguous())
 
 
+FUSE_SHARED = os.environ.get("CERNELS_QWEN3_FUSE_SHARED", "1") != "0"
+
+
 def fused_shared_supported(block) -> bool:
     se = block.shared_expert
-    return se.gate_proj.weight.shape[0] == block.experts.gate_up_proj.shape[1] // 2
+    return FUSE_SHARED and se.gate_proj.weight.shape[0] == block.experts.gate_up_proj.shape[1] // 2
 
 
 def kernel(x, block):
