@@ -35,8 +35,10 @@ __global__ void __launch_bounds__(kRouterWarps * 32) router_topk_kernel(const T*
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int t = blockIdx.x * kRouterWarps + warp;
   if (t >= tokens) return;
-  // With a shared-gate column, logits rows hold experts + 1 values (the last is the gate).
-  const T* row = logits + static_cast<size_t>(t) * (experts + shared_gate);
+  // With a shared-gate column, logits rows hold experts + 1 values (the last is the gate),
+  // padded to a multiple of 8 columns (16-byte rows for the router GEMM).
+  const int row_stride = shared_gate ? ((experts + 1 + 7) / 8) * 8 : experts;
+  const T* row = logits + static_cast<size_t>(t) * row_stride;
   const int out_stride = topk + shared_gate;
   float v[kPerLane];
 #pragma unroll

@@ -292,15 +292,18 @@ ROUTER_TOPK_SOFTMAX = 0
 ROUTER_SOFTMAX_TOPK = 1
 
 
-def router_topk(logits: torch.Tensor, topk: int, mode: int, renorm: bool = False, shared_gate: bool = False):
+def router_topk(logits: torch.Tensor, topk: int, mode: int, renorm: bool = False, shared_gate=False):
     """Top-k expert ids (int32) and fp32 routing weights from router logits [T, E] in one launch
-    (see cernels_router_topk in include/cernels_b200.h). With shared_gate the last logits column
-    is a shared expert's gate: outputs get a (E, sigmoid(gate)) slot appended."""
+    (see cernels_router_topk in include/cernels_b200.h). With shared_gate = E (the routed expert
+    count), logits are [T, pad8(E + 1)] with column E a shared expert's gate: outputs get an
+    (E, sigmoid(gate)) slot appended."""
     _check(logits.is_cuda and logits.dim() == 2 and logits.dtype in (torch.bfloat16, torch.float32),
            "logits must be a [T, E] bf16 or fp32 CUDA tensor")
     logits = logits.contiguous()
     T, E = logits.shape
-    E -= int(bool(shared_gate))
+    if shared_gate:  # [T, pad8(E + 1)]: E routed logits, the gate logit, zero padding
+        E = int(shared_gate) if not isinstance(shared_gate, bool) else E - 1
+        _check(logits.shape[1] == (E + 1 + 7) // 8 * 8, "shared-gate logits must have pad8(E + 1) columns")
     cols = topk + int(bool(shared_gate))
     idx = torch.empty(T, cols, dtype=torch.int32, device=logits.device)
     w = torch.empty(T, cols, dtype=torch.float32, device=logits.device)

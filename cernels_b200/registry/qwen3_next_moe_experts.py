@@ -52,10 +52,20 @@ def route(xf, block):
 
 
 def _router_and_gate(block):
-    """[E + 1, H]: router weight with the shared-expert gate row appended (cached)."""
+    """[pad8(E + 1), H]: router weight, the shared-expert gate row, zero rows up to a multiple of
+    8 (so the router GEMM's output rows stay 16-byte aligned). Cached on the block."""
     g, sg = block.gate.weight, block.shared_expert_gate.weight
     stamp = (g.data_ptr(), g._version, sg.data_ptr(), sg._version)
-    return module_cache(block, "router_gate", stamp, lambda: torch.cat([g.data, sg.data], dim=0).contiguous())
+
+    def build():
+        E = g.shape[0]
+        rows = (E + 1 + 7) // 8 * 8
+        w = torch.zeros(rows, g.shape[1], dtype=g.dtype, device=g.device)
+        w[:E] = g.data
+        w[E] = sg.data[0]
+        return w
+
+    return module_cache(block, "router_gate", stamp, build)
 
 
 FUSE_SHARED = os.environ.get("CERNELS_QWEN3_FUSE_SHARED", "1") != "0"
@@ -79,7 +89,7 @@ def kernel(x, block):
             # the shared expert as an always-on group of the same grouped GEMMs
             logits = torch.nn.functional.linear(xf, _router_and_gate(block))
             idx, w = ops.router_topk(logits, k, ops.ROUTER_SOFTMAX_TOPK, bool(block.gate.norm_topk_prob),
-                                     shared_gate=True)
+                                     shared_gate=int(e.gate_up_proj.shape[0]))
             sw1, sw2 = _shared_weights(block)
             out = ops.run_experts_shared(xf, e.gate_up_proj.data.contiguous(), e.down_proj.data.contiguous(), sw1,
                                          sw2, idx, w, k)

@@ -137,7 +137,8 @@ int cernels_moe_grouped_experts(const cernels_moe_shape* shape, int32_t groups, 
 int cernels_router_topk(const void* logits, int32_t logits_bf16, int32_t tokens, int32_t experts, int32_t topk,
                         int32_t mode, int32_t renorm, int32_t shared_gate, int32_t* indices, float* weights,
                         void* stream);
-/* shared_gate != 0: logits rows hold E + 1 values, the last being a shared expert's gate logit;
+/* shared_gate != 0: logits rows hold E + 1 values (row stride padded to a multiple of 8), column
+ * E being a shared expert's gate logit;
  * indices / weights get topk + 1 columns, the last = (E, sigmoid(gate logit)) — the input of
  * cernels_moe_experts_shared. */
 

@@ -377,7 +377,7 @@ def test_shared_expert_fused_path_matches_separate_path():
     assert qn.fused_shared_supported(blk)
     with torch.no_grad():
         logits = torch.nn.functional.linear(xf, qn._router_and_gate(blk))
-        idx, w = ops.router_topk(logits, k, ops.ROUTER_SOFTMAX_TOPK, True, shared_gate=True)
+        idx, w = ops.router_topk(logits, k, ops.ROUTER_SOFTMAX_TOPK, True, shared_gate=cfg.experts)
         assert torch.all(idx[:, k] == cfg.experts)
         sw1, sw2 = qn._shared_weights(blk)
         e = blk.experts
