@@ -387,3 +387,26 @@ def test_shared_expert_fused_path_matches_separate_path():
         shared = ops.qwen3_next_moe_experts(xf, sw1, sw2, torch.zeros_like(idx[:, :1]), w[:, k:].contiguous(), 1)
         ref = (routed.float() + shared.float()).cpu().numpy()
     assert_close(fused, ref)
+
+
+@pytest.mark.parametrize("name", ["deepseek_v2_lite", "gpt_oss_20b"])
+def test_in_model_swap_matches_module(name):
+    """swaps.SWAPS on transformers experts modules: decode (<= 4 tokens) and prefill shapes."""
+    from cernels_b200 import swaps
+    from cernels_b200.hf_modules import build_module
+    cfg = CONFIGS[name].scaled(tokens=64, experts=8, hidden=512, inter=256)
+    case = make_case(cfg, device=DEV)
+    kind, mod = build_module(case)
+    experts = mod.experts if kind == "gpt_oss" else mod
+    family = "gpt_oss" if kind == "gpt_oss" else "deepseek_v2"
+    for T in (3, 64):
+        x = case.x[:T].contiguous()
+        idx = case.indices[:T].contiguous()
+        w = case.weights[:T].to(torch.bfloat16 if kind != "gpt_oss" else torch.float32).contiguous()
+        with torch.no_grad():
+            swaps.SWAPS[family][0](experts, "stock")
+            ref = experts(x, idx, w)
+            swaps.SWAPS[family][0](experts, "custom")
+            out = experts(x, idx, w)
+            swaps.SWAPS[family][0](experts, "stock")
+        assert torch.allclose(out.float(), ref.float(), atol=2e-2, rtol=2e-2)
