@@ -37,6 +37,7 @@ if ROOT not in sys.path:
     sys.path.insert(0, ROOT)
 
 DEFAULT_CONFIG = "gpt_oss_20b"
+CONFIGS_TOKENS = {"gpt_oss_20b": 16384}  # workloads whose ncu traffic is recorded below
 EP_CONFIGS = ("qwen3_next", "gpt_oss_20b")
 L2_FLUSH_BYTES = 256 << 20
 
@@ -334,6 +335,14 @@ def load_peaks():
         return 6650.0, 1590.0, "fallback"
 
 
+# dram__bytes_read.sum + dram__bytes_write.sum per launch from one ncu capture at the full
+# workload (profiles/grouped_gemm_gpt_oss_20b.md): (config, kernel) -> bytes
+NCU_TRAFFIC = {
+    ("gpt_oss_20b", "gate_up_gemm"): 1.440748e9 + 0.361273e9,
+    ("gpt_oss_20b", "down_gemm"): 0.909377e9 + 0.354875e9,
+}
+
+
 def roofline(cfg, case, stage_ms):
     """Dominant kernel's achieved rate vs the measured peak."""
     from cernels_b200.configs import LAYOUT_GPTOSS, touched_experts
@@ -365,7 +374,7 @@ def roofline(cfg, case, stage_ms):
     r["frac"] = round(achieved / r["peak"], 4)
     r["kernel"] = names[dom]
     r["peak_source"] = src
-    r["traffic"] = None
+    r["traffic"] = NCU_TRAFFIC.get((cfg.name, names[dom])) if cfg.tokens == CONFIGS_TOKENS.get(cfg.name) else None
     r["stage_ms"] = {n: round(v, 4) for n, v in zip(names, stage_ms)}
     r["algorithmic"] = {"flops": flops, "bytes": bytes_}
     return r

@@ -120,6 +120,28 @@ def moe_experts(x, w1, w2, indices, weights, layout=LAYOUT_LINEAR, b1=None, b2=N
     return out
 
 
+def router_tail(logits: np.ndarray, topk: int, mode: int, renorm: bool = False):
+    """Router tail restated from the transformers routers the reference loaders call
+    (src/kops/registry/gpt_oss_moe_experts.py:35, src/kops/registry/qwen3_next_moe_experts.py:28):
+    mode 0 (gpt-oss, transformers models/gpt_oss/modeling_gpt_oss.py:117-131): top-k of the logits,
+    softmax over the k values; mode 1 (qwen3-next, models/qwen3_next/modeling_qwen3_next.py:761-780):
+    softmax over all experts, top-k, optional renormalisation. Ties go to the lower expert id.
+    Returns (indices [T, k] int64, weights [T, k] float32)."""
+    logits = np.asarray(logits, dtype=np.float64)
+    order = np.argsort(-logits, axis=1, kind="stable")[:, :topk]
+    if mode == 0:
+        v = np.take_along_axis(logits, order, axis=1)
+        e = np.exp(v - v[:, :1])
+        w = e / e.sum(axis=1, keepdims=True)
+    else:
+        p = np.exp(logits - logits.max(axis=1, keepdims=True))
+        p = p / p.sum(axis=1, keepdims=True)
+        w = np.take_along_axis(p, order, axis=1)
+        if renorm:
+            w = w / w.sum(axis=1, keepdims=True)
+    return order, w.astype(np.float32)
+
+
 def shared_expert(x, gate_proj, up_proj, down_proj, gate_w):
     """Qwen3-Next always-on shared expert: sigmoid(x @ g^T) * (silu(x Wg^T) * (x Wu^T)) Wd^T
     (src/kops/registry/qwen3_next_moe_experts.py:41-43). Returns float32 [T, H]."""

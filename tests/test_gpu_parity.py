@@ -410,3 +410,17 @@ def test_in_model_swap_matches_module(name):
             out = experts(x, idx, w)
             swaps.SWAPS[family][0](experts, "stock")
         assert torch.allclose(out.float(), ref.float(), atol=2e-2, rtol=2e-2)
+
+
+
+@pytest.mark.parametrize("mode,E,k,renorm", [(0, 32, 4, False), (1, 512, 10, True), (0, 64, 6, False)])
+def test_router_topk_matches_oracle(mode, E, k, renorm):
+    """router_topk kernel vs the numpy router-tail oracle (fp32 logits, no ties)."""
+    g = torch.Generator().manual_seed(100 + E)
+    logits = torch.randn(513, E, generator=g)
+    idx, w = ops.router_topk(logits.to(DEV), k, mode, renorm)
+    r_idx, r_w = O.router_tail(logits.numpy(), k, mode, renorm)
+    assert np.array_equal(idx.cpu().numpy(), r_idx)
+    if mode == 0:  # the kernel rounds gpt-oss scores to bf16 as transformers does
+        r_w = torch.from_numpy(r_w).to(torch.bfloat16).float().numpy()
+    assert np.allclose(w.cpu().numpy(), r_w, atol=1e-5, rtol=1e-2)

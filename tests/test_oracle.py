@@ -66,3 +66,23 @@ def test_route_expert_sets_match_eager_loop():
         _, token_idx = torch.where(mask[e])
         ours = order[offsets[e]:offsets[e + 1]] // k
         assert sorted(token_idx.tolist()) == sorted(ours.tolist())
+
+
+@pytest.mark.parametrize("name,mode,renorm", [("gpt_oss_small", 0, False), ("qwen3_next_small", 1, True)])
+def test_router_tail_oracle_matches_transformers_router(name, mode, renorm):
+    """The router-tail restatement reproduces the transformers routers' selections and weights
+    (logits recomputed with the same bf16 linear the module ran)."""
+    g = golden_io.load(name)
+    x, W = g["x"], g["router_w"]
+    logits = torch.nn.functional.linear(x, W, g["router_b"] if "router_b" in g else None).float().numpy()
+    k = g["indices"].shape[1]
+    idx, w = O.router_tail(logits, k, mode, renorm)
+    ref_idx = g["indices"].numpy()
+    # same expert sets per token (transformers' top-k order among equal values is unspecified)
+    assert all(set(a) == set(b) for a, b in zip(idx.tolist(), ref_idx.tolist()))
+    ref_w = g["weights"].numpy()
+    for t in range(idx.shape[0]):
+        mine = dict(zip(idx[t].tolist(), w[t].tolist()))
+        theirs = dict(zip(ref_idx[t].tolist(), ref_w[t].tolist()))
+        for e, v in theirs.items():
+            assert abs(mine[e] - v) <= 1e-2 * max(1.0, abs(v))
