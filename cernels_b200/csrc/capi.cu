@@ -28,7 +28,8 @@ template <class F>
 PrefillWorkspace carve_prefill(const cernels_moe_shape& s, void* base, F&& done) {
   Carver c{static_cast<uint8_t*>(base)};
   const size_t tk = static_cast<size_t>(s.tokens) * s.topk;
-  const size_t n_chunks = (tk + kRouteChunk - 1) / kRouteChunk;
+  const size_t chunk = static_cast<size_t>(route_chunk(static_cast<long long>(tk)));
+  const size_t n_chunks = (tk + chunk - 1) / chunk;
   PrefillWorkspace w;
   w.status = c.take<int>(1);
   w.block_counts = c.take<int>(n_chunks * s.experts + 1);

@@ -12,8 +12,11 @@
 
 namespace cernels {
 
-// Routing works on chunks of kRouteChunk flat (token, slot) entries per CTA.
+// Routing works on chunks of flat (token, slot) entries, one CTA per chunk: 256 entries for
+// small batches (more CTAs), kRouteChunk for large ones.
 constexpr int kRouteChunk = 1024;
+constexpr int kRouteSmallChunk = 256;
+inline int route_chunk(long long total) { return total <= 16384 ? kRouteSmallChunk : kRouteChunk; }
 constexpr int kRouteThreads = 256;
 constexpr int kMaxExperts = 2048;
 

@@ -9,7 +9,7 @@
 // Here the order inside an expert is the flat index t*topk+j (a stable counting sort,
 // identical to torch.sort(indices.flatten(), stable=True) restricted to valid ids),
 // computed without global atomics:
-//   1. route_count_kernel  — one CTA per 1024-entry chunk, shared-memory histogram
+//   1. route_count_kernel  — one CTA per chunk (256 or 1024 entries), shared-memory histogram
 //   2. route_scan_kernel   — one CTA: per-expert prefix over chunks, offsets, tile offsets
 //   3. route_place_kernel  — one CTA per chunk; warp __match_any_sync ranks entries of
 //                            the same expert, a cross-warp prefix in shared memory keeps
@@ -20,12 +20,13 @@ namespace cernels {
 namespace {
 
 __global__ void __launch_bounds__(kRouteThreads) route_count_kernel(const int32_t* __restrict__ indices, int total,
-                                                                    int experts, int* __restrict__ block_counts) {
+                                                                    int chunk, int experts,
+                                                                    int* __restrict__ block_counts) {
   extern __shared__ int hist[];
   for (int e = threadIdx.x; e < experts; e += blockDim.x) hist[e] = 0;
   __syncthreads();
-  const int base = blockIdx.x * kRouteChunk;
-  const int end = min(base + kRouteChunk, total);
+  const int base = blockIdx.x * chunk;
+  const int end = min(base + chunk, total);
   for (int i = base + threadIdx.x; i < end; i += blockDim.x) {
     const int e = indices[i];
     if (e >= 0 && e < experts) atomicAdd(&hist[e], 1);
@@ -81,11 +82,19 @@ __global__ void __launch_bounds__(1024) route_scan_kernel(int* __restrict__ bloc
     const int e = e0 + threadIdx.x;
     int count = 0;
     if (e < experts) {
-      for (int b = 0; b < n_chunks; ++b) {
-        int* p = block_counts + static_cast<size_t>(b) * experts + e;
-        const int c = *p;
-        *p = count;  // exclusive prefix over chunks, within the expert
-        count += c;
+      // exclusive prefix over chunks, within the expert; loads batched 8 at a time so the
+      // chain of global reads does not serialise on memory latency
+      constexpr int kBatch = 8;
+      for (int b0 = 0; b0 < n_chunks; b0 += kBatch) {
+        int c[kBatch];
+#pragma unroll
+        for (int j = 0; j < kBatch; ++j)
+          c[j] = b0 + j < n_chunks ? block_counts[static_cast<size_t>(b0 + j) * experts + e] : 0;
+#pragma unroll
+        for (int j = 0; j < kBatch; ++j) {
+          if (b0 + j < n_chunks) block_counts[static_cast<size_t>(b0 + j) * experts + e] = count;
+          count += c[j];
+        }
       }
     }
     const int tiles = (count + kBlockM - 1) / kBlockM;
@@ -114,7 +123,7 @@ __global__ void __launch_bounds__(1024) route_scan_kernel(int* __restrict__ bloc
 }
 
 __global__ void __launch_bounds__(kRouteThreads) route_place_kernel(
-    const int32_t* __restrict__ indices, const float* __restrict__ weights, int total, int topk, int experts,
+    const int32_t* __restrict__ indices, const float* __restrict__ weights, int total, int chunk, int topk, int experts,
     const int* __restrict__ chunk_base, int* __restrict__ perm_flat, int* __restrict__ perm_token,
     float* __restrict__ perm_weight, int* __restrict__ inv) {
   constexpr int kWarps = kRouteThreads / 32;
@@ -126,10 +135,10 @@ __global__ void __launch_bounds__(kRouteThreads) route_place_kernel(
 
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int* base_row = chunk_base + static_cast<size_t>(blockIdx.x) * experts;
-  const int chunk0 = blockIdx.x * kRouteChunk;
+  const int chunk0 = blockIdx.x * chunk;
   const unsigned lanes_below = (1u << lane) - 1u;
 
-  for (int r0 = 0; r0 < kRouteChunk; r0 += kRouteThreads) {
+  for (int r0 = 0; r0 < chunk; r0 += kRouteThreads) {
     const int i = chunk0 + r0 + threadIdx.x;
     int e = -1;
     if (i < total) {
@@ -176,7 +185,8 @@ __global__ void __launch_bounds__(kRouteThreads) route_place_kernel(
 cudaError_t launch_route(const int32_t* indices, const float* weights, int tokens, int topk, int experts,
                          const PrefillWorkspace& ws, cudaStream_t stream) {
   const int total = tokens * topk;
-  const int n_chunks = (total + kRouteChunk - 1) / kRouteChunk;
+  const int chunk = route_chunk(total);
+  const int n_chunks = (total + chunk - 1) / chunk;
   const size_t hist_smem = static_cast<size_t>(experts) * sizeof(int);
   const size_t place_smem = static_cast<size_t>(experts) * (kRouteThreads / 32 + 1) * sizeof(int);
   cudaError_t err;
@@ -186,14 +196,15 @@ cudaError_t launch_route(const int32_t* indices, const float* weights, int token
     if (err != cudaSuccess) return err;
   }
   if (n_chunks > 0) {
-    route_count_kernel<<<n_chunks, kRouteThreads, hist_smem, stream>>>(indices, total, experts, ws.block_counts);
+    route_count_kernel<<<n_chunks, kRouteThreads, hist_smem, stream>>>(indices, total, chunk, experts,
+                                                                       ws.block_counts);
   }
   route_scan_kernel<<<1, 1024, hist_smem, stream>>>(ws.block_counts, n_chunks, experts, ws.offsets,
                                                     ws.mtile_offsets);
   if (n_chunks > 0) {
     route_place_kernel<<<n_chunks, kRouteThreads, place_smem, stream>>>(
-        indices, weights, total, topk, experts, ws.block_counts, ws.perm_flat, ws.perm_token, ws.perm_weight,
-        ws.inv);
+        indices, weights, total, chunk, topk, experts, ws.block_counts, ws.perm_flat, ws.perm_token,
+        ws.perm_weight, ws.inv);
   }
   return cudaGetLastError();
 }
