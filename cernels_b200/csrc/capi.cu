@@ -53,8 +53,10 @@ DecodeWorkspace carve_decode(const cernels_moe_shape& s, void* base, F&& done) {
   DecodeWorkspace w;
   w.status = c.take<int>(1);
   w.counters = c.take<int>(static_cast<size_t>(s.hidden) + 8);
+  const DecodeSplits sp = decode_splits(s.tokens, s.topk, s.experts, s.hidden, s.intermediate, s.layout);
   w.glu = c.take<float>(tk * s.intermediate + 4);
-  w.partial = c.take<float>(tk * s.hidden + 4);
+  w.partial = c.take<float>(static_cast<size_t>(sp.s2) * tk * s.hidden + 4);
+  w.pre = sp.s1 > 1 ? c.take<float>(static_cast<size_t>(sp.s1) * tk * 2 * s.intermediate + 4) : nullptr;
   done(c.off);
   return w;
 }

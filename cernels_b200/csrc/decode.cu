@@ -218,20 +218,24 @@ __global__ void __launch_bounds__(kDecThreads) decode_gate_up_linear(
 }
 
 // Last-arriving CTA of an output block combines the partial rows of every token.
+// `partial` holds `splits` slabs of [total, H] (down-projection partial sums over disjoint
+// K ranges); the last of `arrivals` CTAs of this output block sums, per output element,
+// slot by slot and within a slot slab by slab, so the result does not depend on timing.
 __device__ void finish_block(const float* __restrict__ partial, const int32_t* __restrict__ indices,
                              const float* __restrict__ weights, int tokens, int topk, int experts, int H, int c0,
-                             int c1, int n_groups, int* __restrict__ counters, __nv_bfloat16* __restrict__ out,
-                             int* flag) {
+                             int c1, int arrivals, int splits, int* __restrict__ counters,
+                             __nv_bfloat16* __restrict__ out, int* flag) {
   __threadfence();
   __syncthreads();
   if (threadIdx.x == 0) {
     const int prev = atomicAdd(&counters[blockIdx.x], 1);
-    *flag = prev == n_groups - 1;
+    *flag = prev == arrivals - 1;
   }
   __syncthreads();
   if (!*flag) return;
   __threadfence();
   const int width = c1 - c0;
+  const size_t slab = static_cast<size_t>(tokens) * topk * H;
   for (int i = threadIdx.x; i < tokens * width; i += blockDim.x) {
     const int t = i / width, c = c0 + (i - t * width);
     float s = 0.f;
@@ -239,7 +243,10 @@ __device__ void finish_block(const float* __restrict__ partial, const int32_t* _
       const int p = t * topk + j;
       const int e = indices[p];
       if (e < 0 || e >= experts) continue;
-      s = fmaf(weights[p], __ldcg(partial + static_cast<size_t>(p) * H + c), s);
+      const float* src = partial + static_cast<size_t>(p) * H + c;
+      float v = __ldcg(src);
+      for (int z = 1; z < splits; ++z) v += __ldcg(src + z * slab);
+      s = fmaf(weights[p], v, s);
     }
     out[static_cast<size_t>(t) * H + c] = __float2bfloat16_rn(s);
   }
@@ -250,7 +257,7 @@ __device__ void finish_block(const float* __restrict__ partial, const int32_t* _
 // zero rows: CTA row 0 writes zeros when there is no group.
 __device__ void zero_block_if_empty(const Grouping& gr, int tokens, int H, int c0, int c1,
                                     __nv_bfloat16* __restrict__ out) {
-  if (gr.n_groups != 0 || blockIdx.y != 0) return;
+  if (gr.n_groups != 0 || blockIdx.y != 0 || blockIdx.z != 0) return;
   const int width = c1 - c0;
   for (int i = threadIdx.x; i < tokens * width; i += blockDim.x) {
     const int t = i / width, c = c0 + (i - t * width);
@@ -323,25 +330,38 @@ __global__ void __launch_bounds__(kDecThreads) decode_down_linear(
       }
     }
   }
-  finish_block(partial, indices, weights, tokens, topk, experts, H, c0, c1, gr.n_groups, counters, out,
+  finish_block(partial, indices, weights, tokens, topk, experts, H, c0, c1, gr.n_groups, 1, counters, out,
                scratch + 3);
 }
 
+// Rows of one K split, rounded up to 4 floats so the reduction buffer after the operand
+// rows stays 16-byte aligned.
+__host__ __device__ inline int split_rows(int k, int splits) { return (((k + splits - 1) / splits) + 3) & ~3; }
+
 // ---------------------------------------------------------------- GPTOSS gate/up
-// W1[e] is [H, 2F] (columns interleaved gate/up). CTA covers 256 weight columns
-// (128 glu columns); lane owns 8 adjacent columns; warps split the H rows.
+// W1[e] is [H, 2F] (columns interleaved gate/up). CTA (column block, group, K split)
+// covers 256 weight columns (128 glu columns) over the rows [k0, k1) of its split; lane
+// owns 8 adjacent columns; warps split the rows. Each warp issues kUnroll independent
+// 16-byte loads before it consumes them, so a CTA keeps 8 x kUnroll x 512 B in flight.
+// splits == 1: writes glu = act(sum + b1) directly. splits > 1: writes the raw split sums
+// to pre[z, pair, 2F]; the down kernel adds them in split order, adds b1 and applies act.
+template <int kTB>
 __global__ void __launch_bounds__(kDecThreads) decode_gate_up_gptoss(
     const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ w1, const float* __restrict__ b1,
-    const int32_t* __restrict__ indices, int total, int topk, int experts, int H, int F, float* __restrict__ glu,
-    int* __restrict__ counters, int n_counters) {
+    const int32_t* __restrict__ indices, int total, int topk, int experts, int H, int F, int splits,
+    float* __restrict__ glu, float* __restrict__ pre, int* __restrict__ counters, int n_counters) {
+  constexpr int kUnroll = kTB == 8 ? 4 : 8;  // 8 tokens: 64 accumulators leave room for 4 loads
   extern __shared__ __align__(16) int dsm[];
   unsigned* bitmap = reinterpret_cast<unsigned*>(dsm);
   int* list = dsm + kBitmapWords;
   int* scratch = list + kDecodeMaxPairs;
-  float* xs = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(dsm) + kHeaderBytes);  // [kTokBatch, H]
-  float* red = xs + kTokBatch * H;  // [kDecWarps, kColsPerCta]
+  const int k0 = static_cast<int>((static_cast<long long>(H) * blockIdx.z) / splits);
+  const int k1 = static_cast<int>((static_cast<long long>(H) * (blockIdx.z + 1)) / splits);
+  const int kr = k1 - k0;
+  float* xs = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(dsm) + kHeaderBytes);  // [kTB, kr]
+  float* red = xs + kTB * split_rows(H, splits);  // [kDecWarps, kColsPerCta]
 
-  if (blockIdx.x == 0 && blockIdx.y == 0)
+  if (blockIdx.x == 0 && blockIdx.y == 0 && blockIdx.z == 0)
     for (int i = threadIdx.x; i < n_counters; i += blockDim.x) counters[i] = 0;
   const Grouping gr = build_group(indices, total, experts, blockIdx.y, bitmap, list, scratch);
   if (gr.expert < 0) return;
@@ -349,39 +369,52 @@ __global__ void __launch_bounds__(kDecThreads) decode_gate_up_gptoss(
   const int two_f = 2 * F;
   const int col = blockIdx.x * kColsPerCta + lane * 8;  // first of this lane's 8 columns
   const bool col_ok = col < two_f;
-  const __nv_bfloat16* wbase = w1 + static_cast<size_t>(gr.expert) * H * two_f;
+  const __nv_bfloat16* wbase = w1 + static_cast<size_t>(gr.expert) * H * two_f + col;
 
-  for (int p0 = 0; p0 < gr.n_pairs; p0 += kTokBatch) {
-    const int nb = min(kTokBatch, gr.n_pairs - p0);
+  for (int p0 = 0; p0 < gr.n_pairs; p0 += kTB) {
+    const int nb = min(kTB, gr.n_pairs - p0);
     __syncthreads();
-    for (int i = threadIdx.x; i < nb * H; i += blockDim.x) {
-      const int r = i / H, k = i - r * H;
-      xs[r * H + k] = __bfloat162float(x[static_cast<size_t>(list[p0 + r] / topk) * H + k]);
+    for (int i = threadIdx.x; i < nb * kr; i += blockDim.x) {
+      const int r = i / kr, k = i - r * kr;
+      xs[r * kr + k] = __bfloat162float(x[static_cast<size_t>(list[p0 + r] / topk) * H + k0 + k]);
     }
     __syncthreads();
-    float acc[kTokBatch][8];
+    float acc[kTB][8];
 #pragma unroll
-    for (int b = 0; b < kTokBatch; ++b)
+    for (int b = 0; b < kTB; ++b)
 #pragma unroll
       for (int i = 0; i < 8; ++i) acc[b][i] = 0.f;
     if (col_ok) {
-#pragma unroll 4
-      for (int k = warp; k < H; k += kDecWarps) {
-        float wf[8];
-        bf16x8_to_f32(__ldg(reinterpret_cast<const uint4*>(wbase + static_cast<size_t>(k) * two_f + col)), wf);
+      for (int kb = k0 + warp; kb < k1; kb += kDecWarps * kUnroll) {
+        uint4 v[kUnroll];
 #pragma unroll
-        for (int b = 0; b < kTokBatch; ++b) {
-          if (b < nb) {
-            const float xv = xs[b * H + k];
+        for (int u = 0; u < kUnroll; ++u) {
+          const int k = kb + u * kDecWarps;
+          v[u] = k < k1 ? __ldg(reinterpret_cast<const uint4*>(wbase + static_cast<size_t>(k) * two_f))
+                        : make_uint4(0u, 0u, 0u, 0u);
+        }
 #pragma unroll
-            for (int i = 0; i < 8; ++i) acc[b][i] = fmaf(wf[i], xv, acc[b][i]);
+        for (int u = 0; u < kUnroll; ++u) {
+          const int k = kb + u * kDecWarps;
+          if (k < k1) {
+            float wf[8];
+            bf16x8_to_f32(v[u], wf);
+#pragma unroll
+            for (int b = 0; b < kTB; ++b) {
+              if (b < nb) {
+                const float xv = xs[b * kr + (k - k0)];
+#pragma unroll
+                for (int i = 0; i < 8; ++i) acc[b][i] = fmaf(wf[i], xv, acc[b][i]);
+              }
+            }
           }
         }
       }
     }
     for (int b = 0; b < nb; ++b) {
-#pragma unroll
-      for (int i = 0; i < 8; ++i) red[warp * kColsPerCta + lane * 8 + i] = acc[b][i];
+      float4* rw = reinterpret_cast<float4*>(red + warp * kColsPerCta + lane * 8);
+      rw[0] = make_float4(acc[b][0], acc[b][1], acc[b][2], acc[b][3]);
+      rw[1] = make_float4(acc[b][4], acc[b][5], acc[b][6], acc[b][7]);
       __syncthreads();
       // 128 glu outputs per CTA: thread i < 128 reduces the (gate, up) column pair i.
       if (threadIdx.x < kColsPerCta / 2) {
@@ -394,11 +427,17 @@ __global__ void __launch_bounds__(kDecThreads) decode_gate_up_gptoss(
             g += red[w * kColsPerCta + c];
             u += red[w * kColsPerCta + c + 1];
           }
-          if (b1) {
-            g += b1[static_cast<size_t>(gr.expert) * two_f + wc];
-            u += b1[static_cast<size_t>(gr.expert) * two_f + wc + 1];
+          const int pair = list[p0 + b];
+          if (splits == 1) {
+            if (b1) {
+              g += b1[static_cast<size_t>(gr.expert) * two_f + wc];
+              u += b1[static_cast<size_t>(gr.expert) * two_f + wc + 1];
+            }
+            glu[static_cast<size_t>(pair) * F + wc / 2] = act_gptoss(g, u);
+          } else {
+            *reinterpret_cast<float2*>(pre + (static_cast<size_t>(blockIdx.z) * total + pair) * two_f + wc) =
+                make_float2(g, u);
           }
-          glu[static_cast<size_t>(list[p0 + b]) * F + wc / 2] = act_gptoss(g, u);
         }
       }
       __syncthreads();
@@ -407,17 +446,28 @@ __global__ void __launch_bounds__(kDecThreads) decode_gate_up_gptoss(
 }
 
 // ---------------------------------------------------------------- GPTOSS down
-// W2[e] is [F, H]. CTA covers 256 output columns; warps split the F rows.
+// W2[e] is [F, H]. CTA (column block, group, K split) covers 256 output columns over the
+// rows [f0, f1) of its split; warps split the rows. Its glu operand is built in shared
+// memory: glu[pair, f0:f1] (gate/up splits == 1) or act(sum_z pre[z, pair, 2f..2f+1] + b1)
+// (gate/up splits > 1, summed in split order). Down partial sums go to
+// partial[z, pair, H] (b2 added by split 0); the last of the n_groups x splits CTAs of a
+// column block writes the combined bf16 rows.
+template <int kTB>
 __global__ void __launch_bounds__(kDecThreads) decode_down_gptoss(
-    const float* __restrict__ glu, const __nv_bfloat16* __restrict__ w2, const float* __restrict__ b2,
-    const int32_t* __restrict__ indices, const float* __restrict__ weights, int tokens, int topk, int experts, int H,
-    int F, float* __restrict__ partial, int* __restrict__ counters, __nv_bfloat16* __restrict__ out) {
+    const float* __restrict__ glu, const float* __restrict__ pre, const float* __restrict__ b1, int pre_splits,
+    const __nv_bfloat16* __restrict__ w2, const float* __restrict__ b2, const int32_t* __restrict__ indices,
+    const float* __restrict__ weights, int tokens, int topk, int experts, int H, int F, int splits,
+    float* __restrict__ partial, int* __restrict__ counters, __nv_bfloat16* __restrict__ out) {
+  constexpr int kUnroll = kTB == 8 ? 4 : 8;  // 8 tokens: 64 accumulators leave room for 4 loads
   extern __shared__ __align__(16) int dsm[];
   unsigned* bitmap = reinterpret_cast<unsigned*>(dsm);
   int* list = dsm + kBitmapWords;
   int* scratch = list + kDecodeMaxPairs;
-  float* gs = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(dsm) + kHeaderBytes);  // [kTokBatch, F]
-  float* red = gs + kTokBatch * F;  // [kDecWarps, kColsPerCta]
+  const int f0 = static_cast<int>((static_cast<long long>(F) * blockIdx.z) / splits);
+  const int f1 = static_cast<int>((static_cast<long long>(F) * (blockIdx.z + 1)) / splits);
+  const int fr = f1 - f0;
+  float* gs = reinterpret_cast<float*>(reinterpret_cast<uint8_t*>(dsm) + kHeaderBytes);  // [kTB, fr]
+  float* red = gs + kTB * split_rows(F, splits);  // [kDecWarps, kColsPerCta]
   const int total = tokens * topk;
   const Grouping gr = build_group(indices, total, experts, blockIdx.y, bitmap, list, scratch);
   const int c0 = blockIdx.x * kColsPerCta, c1 = min(H, c0 + kColsPerCta);
@@ -426,53 +476,85 @@ __global__ void __launch_bounds__(kDecThreads) decode_down_gptoss(
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int col = c0 + lane * 8;
   const bool col_ok = col < H;
-  const __nv_bfloat16* wbase = w2 + static_cast<size_t>(gr.expert) * F * H;
+  const __nv_bfloat16* wbase = w2 + static_cast<size_t>(gr.expert) * F * H + col;
+  const int two_f = 2 * F;
 
-  for (int p0 = 0; p0 < gr.n_pairs; p0 += kTokBatch) {
-    const int nb = min(kTokBatch, gr.n_pairs - p0);
+  for (int p0 = 0; p0 < gr.n_pairs; p0 += kTB) {
+    const int nb = min(kTB, gr.n_pairs - p0);
     __syncthreads();
-    for (int i = threadIdx.x; i < nb * F; i += blockDim.x) {
-      const int r = i / F, k = i - r * F;
-      gs[r * F + k] = glu[static_cast<size_t>(list[p0 + r]) * F + k];
+    for (int i = threadIdx.x; i < nb * fr; i += blockDim.x) {
+      const int r = i / fr, f = f0 + (i - r * fr);
+      const int pair = list[p0 + r];
+      float v;
+      if (pre_splits == 1) {
+        v = glu[static_cast<size_t>(pair) * F + f];
+      } else {
+        const float* src = pre + static_cast<size_t>(pair) * two_f + 2 * f;
+        float2 gu = __ldcg(reinterpret_cast<const float2*>(src));
+        for (int z = 1; z < pre_splits; ++z) {
+          const float2 t = __ldcg(reinterpret_cast<const float2*>(src + static_cast<size_t>(z) * total * two_f));
+          gu.x += t.x;
+          gu.y += t.y;
+        }
+        if (b1) {
+          gu.x += b1[static_cast<size_t>(gr.expert) * two_f + 2 * f];
+          gu.y += b1[static_cast<size_t>(gr.expert) * two_f + 2 * f + 1];
+        }
+        v = act_gptoss(gu.x, gu.y);
+      }
+      gs[r * fr + (f - f0)] = v;
     }
     __syncthreads();
-    float acc[kTokBatch][8];
+    float acc[kTB][8];
 #pragma unroll
-    for (int b = 0; b < kTokBatch; ++b)
+    for (int b = 0; b < kTB; ++b)
 #pragma unroll
       for (int i = 0; i < 8; ++i) acc[b][i] = 0.f;
     if (col_ok) {
-#pragma unroll 4
-      for (int k = warp; k < F; k += kDecWarps) {
-        float wf[8];
-        bf16x8_to_f32(__ldg(reinterpret_cast<const uint4*>(wbase + static_cast<size_t>(k) * H + col)), wf);
+      for (int kb = f0 + warp; kb < f1; kb += kDecWarps * kUnroll) {
+        uint4 v[kUnroll];
 #pragma unroll
-        for (int b = 0; b < kTokBatch; ++b) {
-          if (b < nb) {
-            const float gv = gs[b * F + k];
+        for (int u = 0; u < kUnroll; ++u) {
+          const int k = kb + u * kDecWarps;
+          v[u] = k < f1 ? __ldg(reinterpret_cast<const uint4*>(wbase + static_cast<size_t>(k) * H))
+                        : make_uint4(0u, 0u, 0u, 0u);
+        }
 #pragma unroll
-            for (int i = 0; i < 8; ++i) acc[b][i] = fmaf(wf[i], gv, acc[b][i]);
+        for (int u = 0; u < kUnroll; ++u) {
+          const int k = kb + u * kDecWarps;
+          if (k < f1) {
+            float wf[8];
+            bf16x8_to_f32(v[u], wf);
+#pragma unroll
+            for (int b = 0; b < kTB; ++b) {
+              if (b < nb) {
+                const float gv = gs[b * fr + (k - f0)];
+#pragma unroll
+                for (int i = 0; i < 8; ++i) acc[b][i] = fmaf(wf[i], gv, acc[b][i]);
+              }
+            }
           }
         }
       }
     }
     for (int b = 0; b < nb; ++b) {
-#pragma unroll
-      for (int i = 0; i < 8; ++i) red[warp * kColsPerCta + lane * 8 + i] = acc[b][i];
+      float4* rw = reinterpret_cast<float4*>(red + warp * kColsPerCta + lane * 8);
+      rw[0] = make_float4(acc[b][0], acc[b][1], acc[b][2], acc[b][3]);
+      rw[1] = make_float4(acc[b][4], acc[b][5], acc[b][6], acc[b][7]);
       __syncthreads();
       const int c = c0 + threadIdx.x;
       if (threadIdx.x < kColsPerCta && c < H) {
         float s = 0.f;
 #pragma unroll
         for (int w = 0; w < kDecWarps; ++w) s += red[w * kColsPerCta + threadIdx.x];
-        if (b2) s += b2[static_cast<size_t>(gr.expert) * H + c];
-        partial[static_cast<size_t>(list[p0 + b]) * H + c] = s;
+        if (b2 && blockIdx.z == 0) s += b2[static_cast<size_t>(gr.expert) * H + c];
+        partial[(static_cast<size_t>(blockIdx.z) * total + list[p0 + b]) * H + c] = s;
       }
       __syncthreads();
     }
   }
-  finish_block(partial, indices, weights, tokens, topk, experts, H, c0, c1, gr.n_groups, counters, out,
-               scratch + 3);
+  finish_block(partial, indices, weights, tokens, topk, experts, H, c0, c1, gr.n_groups * splits, splits, counters,
+               out, scratch + 3);
 }
 
 // ---------------------------------------------------------------- grouping for the streaming kernel
@@ -969,6 +1051,52 @@ __global__ void __launch_bounds__(kStreamThreads, 1) decode_stream_linear(
 
 }  // namespace
 
+template <int kTB>
+cudaError_t launch_gptoss(const DecodeArgs& a, const DecodeWorkspace& ws, const DecodeSplits& sp, int max_groups,
+                          cudaStream_t stream) {
+  const int H = a.hidden, F = a.inter, total = a.tokens * a.topk;
+  const size_t smem1 = kHeaderBytes + (static_cast<size_t>(kTB) * split_rows(H, sp.s1) + kDecWarps * kColsPerCta) * 4;
+  const size_t smem2 = kHeaderBytes + (static_cast<size_t>(kTB) * split_rows(F, sp.s2) + kDecWarps * kColsPerCta) * 4;
+  const int n_hblocks = (H + kColsPerCta - 1) / kColsPerCta;
+  cudaError_t err;
+  if ((err = cudaFuncSetAttribute(decode_gate_up_gptoss<kTB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  static_cast<int>(smem1))) != cudaSuccess)
+    return err;
+  if ((err = cudaFuncSetAttribute(decode_down_gptoss<kTB>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  static_cast<int>(smem2))) != cudaSuccess)
+    return err;
+  dim3 g1((2 * F + kColsPerCta - 1) / kColsPerCta, max_groups, sp.s1);
+  decode_gate_up_gptoss<kTB><<<g1, kDecThreads, smem1, stream>>>(a.x, a.w1, a.b1, a.indices, total, a.topk,
+                                                                 a.experts, H, F, sp.s1, ws.glu, ws.pre, ws.counters,
+                                                                 n_hblocks);
+  dim3 g2(n_hblocks, max_groups, sp.s2);
+  decode_down_gptoss<kTB><<<g2, kDecThreads, smem2, stream>>>(ws.glu, ws.pre, a.b1, sp.s1, a.w2, a.b2, a.indices,
+                                                              a.weights, a.tokens, a.topk, a.experts, H, F, sp.s2,
+                                                              ws.partial, ws.counters, a.out);
+  return cudaGetLastError();
+}
+
+DecodeSplits decode_splits(int tokens, int topk, int experts, int hidden, int inter, int layout) {
+  DecodeSplits sp{1, 1};
+  const long long total = static_cast<long long>(tokens) * topk;
+  if (layout != CERNELS_LAYOUT_GPTOSS || total <= 0) return sp;
+  const long long groups = total < experts ? total : experts;
+  // About one resident wave on a 148-SM part (3 CTAs per SM; 4 for single-token batches,
+  // whose CTAs are shortest), each split keeping >= 64 rows. Measured on gpt-oss-20b
+  // shapes: 2, 6 and 8 CTAs per SM, or up to 16 splits, were slower.
+  const long long kTargetCtas = (tokens == 1 ? 4 : 3) * 148;
+  constexpr int kMaxSplits = 8;
+  auto pick = [&](long long ctas, int rows) {
+    long long s = (kTargetCtas + ctas - 1) / ctas;
+    if (s > kMaxSplits) s = kMaxSplits;
+    if (s > rows / 64) s = rows / 64;
+    return s < 1 ? 1 : static_cast<int>(s);
+  };
+  sp.s1 = pick(groups * ((2LL * inter + kColsPerCta - 1) / kColsPerCta), hidden);
+  sp.s2 = pick(groups * ((hidden + kColsPerCta - 1) / kColsPerCta), inter);
+  return sp;
+}
+
 cudaError_t launch_decode(const DecodeArgs& a, const DecodeWorkspace& ws, cudaStream_t stream) {
   const int total = a.tokens * a.topk;
   if (a.tokens <= 0) return cudaSuccess;
@@ -1033,21 +1161,17 @@ cudaError_t launch_decode(const DecodeArgs& a, const DecodeWorkspace& ws, cudaSt
     decode_down_linear<<<g2, kDecThreads, smem2, stream>>>(ws.glu, a.w2, a.indices, a.weights, a.tokens, a.topk,
                                                            a.experts, H, F, ws.partial, ws.counters, a.out);
   } else {
-    const size_t smem1 = kHeaderBytes + (static_cast<size_t>(kTokBatch) * H + kDecWarps * kColsPerCta) * 4;
-    const size_t smem2 = kHeaderBytes + (static_cast<size_t>(kTokBatch) * F + kDecWarps * kColsPerCta) * 4;
-    const int n_hblocks = (H + kColsPerCta - 1) / kColsPerCta;
-    if ((err = cudaFuncSetAttribute(decode_gate_up_gptoss, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                    static_cast<int>(smem1))) != cudaSuccess)
-      return err;
-    if ((err = cudaFuncSetAttribute(decode_down_gptoss, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                    static_cast<int>(smem2))) != cudaSuccess)
-      return err;
-    dim3 g1((2 * F + kColsPerCta - 1) / kColsPerCta, max_groups);
-    decode_gate_up_gptoss<<<g1, kDecThreads, smem1, stream>>>(a.x, a.w1, a.b1, a.indices, total, a.topk, a.experts,
-                                                              H, F, ws.glu, ws.counters, n_hblocks);
-    dim3 g2(n_hblocks, max_groups);
-    decode_down_gptoss<<<g2, kDecThreads, smem2, stream>>>(ws.glu, a.w2, a.b2, a.indices, a.weights, a.tokens,
-                                                           a.topk, a.experts, H, F, ws.partial, ws.counters, a.out);
+    const DecodeSplits sp = decode_splits(a.tokens, a.topk, a.experts, H, F, a.layout);
+    // Pairs of one group never exceed the token count (a token picks an expert once), so
+    // the operand batch is sized to it. Results do not depend on the batch size chosen.
+    const int tb = a.tokens >= 8 ? 8 : a.tokens >= 3 ? 4 : a.tokens;
+    switch (tb) {
+      case 1: err = launch_gptoss<1>(a, ws, sp, max_groups, stream); break;
+      case 2: err = launch_gptoss<2>(a, ws, sp, max_groups, stream); break;
+      case 4: err = launch_gptoss<4>(a, ws, sp, max_groups, stream); break;
+      default: err = launch_gptoss<8>(a, ws, sp, max_groups, stream); break;
+    }
+    if (err != cudaSuccess) return err;
   }
   return cudaGetLastError();
 }

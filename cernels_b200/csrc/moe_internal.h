@@ -47,8 +47,17 @@ struct DecodeWorkspace {
   int* status;       // [1]
   int* counters;     // [max(H, F) / 8 + 1] arrival counters of the down stage
   float* glu;        // [Tk, F] fp32 activation rows (flat (token, slot) order)
-  float* partial;    // [Tk, H] fp32 per-pair down-projection rows
+  float* partial;    // [s2, Tk, H] fp32 per-pair down-projection rows, one slab per K split
+  float* pre;        // [s1, Tk, 2F] fp32 gate/up split sums (only when s1 > 1)
 };
+
+// K splits of the GPTOSS decode kernels (gate/up s1, down s2): enough CTAs to keep every
+// SM's load pipeline full when only a few experts are touched. A function of the shape
+// only, so workspace sizing and launch agree.
+struct DecodeSplits {
+  int s1, s2;
+};
+DecodeSplits decode_splits(int tokens, int topk, int experts, int hidden, int inter, int layout);
 
 size_t prefill_workspace_bytes(const cernels_moe_shape& s);
 PrefillWorkspace carve_prefill_workspace(const cernels_moe_shape& s, void* base);

@@ -191,6 +191,27 @@ def test_decode_deterministic():
     assert torch.equal(a, b)
 
 
+@pytest.mark.parametrize("T,H,E,F,k", [(1, 200, 8, 136, 2), (3, 1000, 16, 520, 4), (5, 2880, 32, 2880, 4),
+                                       (2, 4096, 128, 1024, 8)])
+def test_decode_gptoss_split_k_shapes(T, H, E, F, k):
+    """GPTOSS decode splits K across CTAs when few experts are touched (split count from the
+    shape; ragged splits when H or F is not a multiple of it): matches the oracle, and two
+    calls give identical bits."""
+    g = torch.Generator().manual_seed(11 * T + H)
+    x = torch.randn(T, H, generator=g).to(torch.bfloat16)
+    w1 = (torch.randn(E, H, 2 * F, generator=g) * 0.02).to(torch.bfloat16)
+    w2 = (torch.randn(E, F, H, generator=g) * 0.02).to(torch.bfloat16)
+    b1 = torch.randn(E, 2 * F, generator=g) * 0.01
+    b2 = torch.randn(E, H, generator=g) * 0.01
+    idx = torch.stack([torch.randperm(E, generator=g)[:k] for _ in range(T)])
+    w = torch.rand(T, k, generator=g)
+    ref = oracle_out(x, w1, w2, idx, w, LAYOUT_GPTOSS, b1, b2)
+    a = run_op(x, w1, w2, idx, w, k, LAYOUT_GPTOSS, True, b1, b2)
+    b = run_op(x, w1, w2, idx, w, k, LAYOUT_GPTOSS, True, b1, b2)
+    assert_close(a, ref)
+    assert torch.equal(a, b)
+
+
 # ---------------------------------------------------------------- benchmark configurations
 @pytest.mark.parametrize("name", ["deepseek_v2_lite", "qwen3_30b_a3b", "qwen3_next"])
 def test_benchmark_configs_full_size(name):
