@@ -170,8 +170,10 @@ int cernels_moe_experts_profiled(const cernels_moe_shape* shape, const void* x, 
  * the scratch lives in a 4 MiB static __device__ array inside this library, held on each
  * device that loads the library until the process exits. The first call on a device looks
  * up that array's device address (cudaGetSymbolAddress), so make that first call before
- * any stream capture. Problems needing more than 4 MiB of decode scratch (T*topk*(F+H)*4
- * bytes plus a few KB), or T*topk > 1024, return CERNELS_E_UNSUPPORTED. All calls on a
+ * any stream capture. Problems needing more than 4 MiB of decode scratch (the decode
+ * workspace size that cernels_moe_workspace_bytes reports: T*topk*(F+H)*4 bytes plus a few
+ * KB, and for the GPTOSS layout at small T up to 8 K-split slabs of T*topk*(2F) and
+ * T*topk*H fp32 values), or T*topk > 1024, return CERNELS_E_UNSUPPORTED. All calls on a
  * device share the one array: calls whose kernels may overlap on the GPU (different
  * streams, or concurrent host threads) race and must be serialised by the caller. */
 int cernels_moe_experts_decode_noalloc(const cernels_moe_shape* shape, const void* x, const void* gate_up_proj,
