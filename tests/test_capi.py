@@ -49,6 +49,26 @@ def test_workspace_sizes_grow_with_tokens():
     assert _lib.workspace_bytes(shape(T=8), True) > 0
 
 
+def test_gptoss_decode_workspace_holds_k_split_slabs():
+    """GPTOSS decode at a few tokens splits K across CTAs (gpt-oss-20b at T=1: 4 touched experts
+    x 23 gate/up column blocks -> 7 splits; x 12 down column blocks -> 8 splits, capped); the
+    workspace query covers the gate/up split sums and the down split slabs, and the LINEAR
+    layout keeps one slab."""
+    T, H, E, F, k = 1, 2880, 32, 2880, 4
+    tk = T * k
+    gptoss = _lib.workspace_bytes(_lib.MoeShape(T, H, E, F, k, _lib.LAYOUT_GPTOSS), True)
+    linear = _lib.workspace_bytes(_lib.MoeShape(T, H, E, F, k, _lib.LAYOUT_LINEAR), True)
+    assert linear >= tk * (F + H) * 4
+    assert gptoss >= tk * F * 4 + 8 * tk * H * 4 + 7 * tk * 2 * F * 4
+    assert gptoss - linear >= 7 * tk * H * 4 + 7 * tk * 2 * F * 4
+    # 64 tokens: 32 groups x 23 gate/up blocks fill the machine (no gate/up split); 32 x 12 down
+    # blocks do not (2 down splits): exactly one extra [T*topk, H] fp32 slab, up to alignment
+    big = (64, H, E, F, k)
+    extra = (_lib.workspace_bytes(_lib.MoeShape(*big, _lib.LAYOUT_GPTOSS), True)
+             - _lib.workspace_bytes(_lib.MoeShape(*big, _lib.LAYOUT_LINEAR), True))
+    assert 64 * k * H * 4 <= extra <= 64 * k * H * 4 + 1024
+
+
 @pytest.mark.parametrize("bad,code", [
     (dict(H=60), 2), (dict(F=12), 2), (dict(E=0), 1), (dict(k=0), 1), (dict(T=-1), 1), (dict(layout=7), 1),
     (dict(E=4096), 5),
