@@ -12,8 +12,11 @@ launch stream, L2 flushed with a 256 MB write before every timed step, max over 
 ``e2e`` is the same metric through the same public API from pinned host buffers
 (host->device copy of the step's inputs and device->host copy of its output inside the
 timed region). Multi-GPU runs (torchrun, one rank per GPU) use expert parallelism for
-the EP configs (qwen3_next, gpt_oss_20b): tokens and experts sharded contiguously, NCCL
-all-to-all dispatch/combine; total tokens fixed ("strong" scaling).
+the EP configs (qwen3_next, gpt_oss_20b): tokens and experts sharded contiguously, rows
+dispatched to and returned from their experts' owners through NVLink peer memory by this
+library's own kernels (cernels_ep_*; NCCL all-to-all is the optional transport); total
+tokens fixed ("strong" scaling). At N = 1 the line also carries ``configs``: every other
+benchmark configuration (C1, C3, C4, decode shapes) timed the same way.
 
 ``--impl reference`` times the reference's own CPU path — the transformers op_eager
 module the reference benchmarks against — on a bounded token sample on this host's cores.
@@ -53,6 +56,7 @@ def parse_args(argv=None):
     p.add_argument("--cpu-sample-s", type=float, default=15.0, help="target seconds of the CPU baseline sample")
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--graph", action="store_true", help="replay the step as a CUDA graph (decode)")
+    p.add_argument("--no-configs", action="store_true", help="skip the sweep over the other configurations")
     return p.parse_args(argv)
 
 
@@ -298,7 +302,7 @@ def decode_roofline(case, steps):
     import torch
 
     from cernels_b200 import ops
-    from cernels_b200.configs import touched_experts
+    from cernels_b200.configs import LAYOUT_GPTOSS, touched_experts
 
     cfg = case.cfg
     idx = case.indices.to(torch.int32).contiguous()
@@ -322,7 +326,11 @@ def decode_roofline(case, steps):
     bytes_ = 3.0 * cfg.hidden * cfg.inter * 2 * e + 2.0 * cfg.tokens * cfg.hidden * 2
     achieved = bytes_ / (ms / 1e3) / 1e9
     return {"bound": "hbm", "achieved": round(achieved, 1), "peak": hbm, "unit": "GB/s",
-            "frac": round(achieved / hbm, 4), "kernel": "decode op (decode_fused_linear)", "peak_source": src,
+            "frac": round(achieved / hbm, 4),
+            "kernel": "decode op (" + ("split-K GPTOSS decode kernels" if cfg.layout == LAYOUT_GPTOSS else
+                                       "streaming LINEAR decode kernel" if cfg.tokens * cfg.topk <= 12 else
+                                       "two-kernel LINEAR decode") + ")",
+            "peak_source": src,
             "traffic": None, "op_ms": round(ms, 4), "algorithmic": {"bytes": bytes_, "touched_experts": e}}
 
 
@@ -457,7 +465,10 @@ def run_reference(args):
         "scaling": "strong" if cfg.name in EP_CONFIGS else "weak", "vs_baseline": None, "dtype": "bf16",
         "data": "synthetic (seeded, reference config distributions)",
         "config": {"workload": cfg.name, "tokens": cfg.tokens, "hidden": cfg.hidden, "experts": cfg.experts,
-                   "intermediate": cfg.inter, "topk": cfg.topk, "reference_op": f"transformers {type(module).__name__}"},
+                   "intermediate": cfg.inter, "topk": cfg.topk, "reference_op": f"transformers {type(module).__name__}",
+                   "sample_tokens_per_step": n,
+                   "note": "a bounded token sample per step, reported as a per-token rate; the CPU arm "
+                           "does not scale with N"},
         "cpu_baseline": {"value": round(value, 2), "unit": "tokens/s", "cores": _threads(), "kind": "reference",
                          "sample": f"first {n} of {cfg.tokens} tokens per step, transformers {type(module).__name__} "
                                    f"bf16 eager on CPU"},
@@ -534,6 +545,10 @@ def run_ours(args):
         if world == 1 and not args.no_cpu_baseline:
             log("cpu baseline")
             cpu = cpu_oracle_baseline(case, args.cpu_sample_s)
+    configs = None
+    if world == 1 and not args.no_configs:
+        log("configuration sweep")
+        configs = measure_configs(min(args.steps, 10), device)
     if rank == 0:
         line = {
             "metric": "MoE-experts tokens/s", "value": round(value, 1), "unit": "tokens/s", "n_gpus": world,
@@ -551,12 +566,84 @@ def run_ours(args):
             "gpu_launches": launches * args.steps,
             "clocks": clocks.summary(),
             "op_roofline_ms": round(op_roofline_ms(cfg, case), 4),
+            "configs": configs,
         }
         print(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
     return 0
+
+
+# Every benchmark configuration other than the headline one, measured in the same run
+# (N = 1): (label, config, tokens override, decode entry point)
+CONFIG_SWEEP = [
+    ("deepseek_v2_lite", "deepseek_v2_lite", None, False),
+    ("qwen3_30b_a3b", "qwen3_30b_a3b", None, False),
+    ("qwen3_next", "qwen3_next", None, False),
+    ("decode_t1", "decode", 1, True),
+    ("decode_t4", "decode", 4, True),
+    ("decode_t8", "decode", 8, True),
+    ("qwen3_30b_a3b_decode_t8", "qwen3_30b_a3b", 8, True),
+    ("gpt_oss_20b_decode_t1", "gpt_oss_20b", 1, True),
+    ("gpt_oss_20b_decode_t8", "gpt_oss_20b", 8, True),
+]
+
+
+def config_step(kind, module, case, decode):
+    """The reference-facing call of one configuration: (step, inputs)."""
+    import torch
+
+    from cernels_b200.registry import cohere2_moe_experts as c2
+    from cernels_b200.registry import gpt_oss_moe_experts as go
+    from cernels_b200.registry import qwen3_next_moe_experts as qn
+
+    if kind in ("gpt_oss", "qwen3_next"):
+        mod = go if kind == "gpt_oss" else qn
+        fn = mod.decode_kernel if decode else mod.kernel
+        return (lambda xx: fn(xx.unsqueeze(0), module).squeeze(0)), [case.x]
+    fn = c2.decode_kernel if decode else c2.kernel
+    return (lambda xx, ii, ww: fn(xx, ii, ww, module)), [case.x, case.indices, case.weights.to(torch.bfloat16)]
+
+
+def measure_configs(steps, device):
+    """ms/step, tokens/s, op roofline and the dominant kernel's roofline fraction of every
+    configuration in CONFIG_SWEEP, timed like the headline (CUDA events on the launch stream,
+    L2 flushed before every timed step; decode steps replayed as CUDA graphs), with clocks
+    sampled over the whole sweep."""
+    import torch
+
+    from cernels_b200.configs import CONFIGS, make_case
+    from cernels_b200.hf_modules import build_module
+
+    flush = torch.empty(L2_FLUSH_BYTES, dtype=torch.uint8, device=device)
+    out = {}
+    with ClockSampler(device.index or 0) as clocks:
+        for label, name, tokens, decode in CONFIG_SWEEP:
+            try:
+                cfg = CONFIGS[name] if tokens is None else CONFIGS[name].with_tokens(tokens)
+                case = make_case(cfg, device=device)
+                kind, module = build_module(case, device=device)
+                step, inputs = config_step(kind, module, case, decode)
+                total_ms, _ = time_device(step, inputs, steps, 3, flush, graph=decode)
+                ms = total_ms / steps
+                roof = decode_roofline(case, steps) if decode else roofline(cfg, case, stage_profile(case, steps))
+                op_ms = op_roofline_ms(cfg, case)
+                out[label] = {
+                    "tokens": cfg.tokens, "entry": ("decode_kernel" if decode else "kernel"),
+                    "ms_per_step": round(ms, 4), "tokens_per_s": round(cfg.tokens / (ms / 1e3), 1),
+                    "op_roofline_ms": round(op_ms, 4), "frac_of_op_roofline": round(op_ms / ms, 4),
+                    "graph": decode,
+                    "roofline": {k: roof[k] for k in ("bound", "kernel", "achieved", "peak", "unit", "frac")},
+                }
+                del case, module
+            except Exception as e:  # one failing entry must not lose the others
+                out[label] = {"error": f"{type(e).__name__}: {e}"}
+            torch.cuda.synchronize()
+    out["clocks"] = clocks.summary()
+    out["method"] = ("CUDA events on the launch stream, 256 MB L2 flush before every timed step, "
+                     f"{steps} timed steps after 3 warm-up; decode entries replayed as CUDA graphs")
+    return out
 
 
 def op_roofline_ms(cfg, case):

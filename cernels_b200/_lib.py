@@ -41,6 +41,7 @@ _SHAPE_P = ctypes.POINTER(MoeShape)
 PROTOTYPES = {
     "cernels_error_string": (ctypes.c_char_p, [ctypes.c_int]),
     "cernels_version": (ctypes.c_int, []),
+    "cernels_set_wait_limit_ns": (ctypes.c_int, [ctypes.c_uint64]),
     "cernels_moe_workspace_bytes": (ctypes.c_int, [_SHAPE_P, ctypes.c_int, ctypes.POINTER(_SZ)]),
     "cernels_moe_experts": (ctypes.c_int, [_SHAPE_P, _VP, _VP, _VP, _VP, _VP, _VP, _VP, _VP, _VP, _SZ, _VP]),
     "cernels_moe_experts_decode": (ctypes.c_int, [_SHAPE_P, _VP, _VP, _VP, _VP, _VP, _VP, _VP, _VP, _VP, _SZ, _VP]),

@@ -81,6 +81,8 @@ int cuda_rc(cudaError_t e) {
   return CERNELS_E_CUDA;
 }
 
+std::atomic<unsigned long long> g_wait_limit_ns{0};
+
 int sm_count_cached() {
   int dev = 0;
   if (cudaGetDevice(&dev) != cudaSuccess) return 0;
@@ -125,6 +127,11 @@ DecodeWorkspace carve_decode_workspace(const cernels_moe_shape& s, void* base) {
 
 int device_sm_count() { return sm_count_cached(); }
 
+unsigned long long wait_limit_ns(unsigned long long default_ns) {
+  const unsigned long long v = g_wait_limit_ns.load(std::memory_order_relaxed);
+  return v ? v : default_ns;
+}
+
 }  // namespace cernels
 
 using namespace cernels;
@@ -144,7 +151,12 @@ const char* cernels_error_string(int code) {
   return "unknown error";
 }
 
-int cernels_version(void) { return 100; }
+int cernels_version(void) { return 200; }
+
+int cernels_set_wait_limit_ns(uint64_t ns) {
+  g_wait_limit_ns.store(ns, std::memory_order_relaxed);
+  return CERNELS_OK;
+}
 
 int cernels_moe_workspace_bytes(const cernels_moe_shape* shape, int decode, size_t* bytes) {
   const int rc = check_shape(shape);
@@ -311,6 +323,8 @@ int cernels_moe_experts_decode(const cernels_moe_shape* shape, const void* x, co
   if (rc || s.tokens == 0) return rc;
   cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
   const DecodeWorkspace ws = carve_decode_workspace(s, workspace);
+  const cudaError_t zero = cudaMemsetAsync(ws.status, 0, sizeof(int), stream);
+  if (zero != cudaSuccess) return cuda_rc(zero);
   DecodeArgs a{};
   a.x = static_cast<const __nv_bfloat16*>(x);
   a.w1 = static_cast<const __nv_bfloat16*>(gate_up_proj);
@@ -438,7 +452,14 @@ int cernels_workspace_status(const cernels_moe_shape* shape, int decode, const v
                              void* stream_ptr) {
   const int rc = check_shape(shape);
   if (rc) return rc;
-  if (!workspace || !status) return CERNELS_E_NULL;
+  if (!status) return CERNELS_E_NULL;
+  if (!workspace) {
+    // decode with no workspace: the scratch of cernels_moe_experts_decode_noalloc
+    if (!decode) return CERNELS_E_NULL;
+    void* scratch = nullptr;
+    if (const int rc2 = noalloc_scratch(&scratch)) return rc2;
+    workspace = scratch;
+  }
   const int* dev = decode ? carve_decode_workspace(*shape, const_cast<void*>(workspace)).status
                           : carve_prefill_workspace(*shape, const_cast<void*>(workspace)).status;
   cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);

@@ -46,6 +46,9 @@ int scratch_for_current_device(void** out) {
 }
 
 }  // namespace
+
+int noalloc_scratch(void** out) { return scratch_for_current_device(out); }
+
 }  // namespace cernels
 
 using namespace cernels;
@@ -66,8 +69,10 @@ extern "C" int cernels_moe_experts_decode_noalloc(const cernels_moe_shape* shape
   void* scratch = nullptr;
   rc = scratch_for_current_device(&scratch);
   if (rc) return rc;
-  // The decode kernels write every scratch element they later read, and the first
-  // kernel zeroes the arrival counters itself, so nothing has to be cleared here.
+  // The decode kernels write every scratch element they later read, the first kernel
+  // zeroes the arrival counters itself, and the decode entry point clears the status word
+  // (read back with cernels_workspace_status(shape, 1, NULL, ...)), so nothing else has to
+  // be cleared here.
   return cernels_moe_experts_decode(&s, x, gate_up_proj, gate_up_bias, down_proj, down_bias, indices, weights, out,
                                     scratch, kNoAllocScratchBytes, stream);
 }

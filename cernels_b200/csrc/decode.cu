@@ -34,7 +34,6 @@ constexpr int kRowsPerCta = kDecWarps * kRowsPerWarp;  // 16
 constexpr int kColsPerCta = 256;      // GPTOSS: output columns per CTA (32 lanes x 8)
 constexpr float kLimit = 7.0f;
 constexpr float kAlpha = 1.702f;
-constexpr unsigned long long kBarrierLimitNs = 2000000000ull;
 
 __device__ __forceinline__ unsigned long long global_timer_ns_dec() {
   unsigned long long t;
@@ -635,8 +634,9 @@ __device__ void build_groups_fused(const int32_t* __restrict__ indices, int tota
 }
 
 // Grid-wide barrier for a cooperative launch. bar[0] = arrivals, bar[1] = generation.
-// Bounded: gives up after kWaitLimitNs, records `code` in *status and returns false.
-__device__ bool grid_barrier_bounded(unsigned* bar, unsigned n_blocks, int* status, int code, int* flag) {
+// Bounded: gives up after limit_ns, records `code` in *status and returns false.
+__device__ bool grid_barrier_bounded(unsigned* bar, unsigned n_blocks, int* status, int code, int* flag,
+                                     unsigned long long limit_ns) {
   __syncthreads();
   if (threadIdx.x == 0) {
     *flag = 1;
@@ -651,7 +651,7 @@ __device__ bool grid_barrier_bounded(unsigned* bar, unsigned n_blocks, int* stat
     } else {
       const unsigned long long t0 = global_timer_ns_dec();
       while (*vgen == gen) {
-        if (global_timer_ns_dec() - t0 > kBarrierLimitNs) {
+        if (global_timer_ns_dec() - t0 > limit_ns) {
           if (status) atomicCAS(status, 0, code);
           *flag = 0;
           break;
@@ -797,7 +797,7 @@ __global__ void __launch_bounds__(kStreamThreads, 1) decode_stream_linear(
     const __nv_bfloat16* __restrict__ x, const __nv_bfloat16* __restrict__ w1, const __nv_bfloat16* __restrict__ w2,
     const int32_t* __restrict__ indices, const float* __restrict__ weights, int tokens, int topk, int experts, int H,
     int F, float* __restrict__ glu, float* __restrict__ partial, unsigned* __restrict__ barrier,
-    int* __restrict__ status, __nv_bfloat16* __restrict__ out) {
+    int* __restrict__ status, __nv_bfloat16* __restrict__ out, unsigned long long wait_ns) {
   extern __shared__ __align__(128) uint8_t dsm_raw[];
   StreamShared& S = *reinterpret_cast<StreamShared*>(dsm_raw);
   uint8_t* ring = dsm_raw + ((sizeof(StreamShared) + 127) & ~size_t(127));
@@ -841,11 +841,19 @@ __global__ void __launch_bounds__(kStreamThreads, 1) decode_stream_linear(
   const int u2_end = static_cast<int>((static_cast<long long>(units2) * (blockIdx.x + 1)) / gridDim.x);
   int stage = 0;
   uint32_t phase = 0;
+  long long issued = 0;  // producer: stages loaded so far
   auto advance = [&]() {
+    ++issued;
     if (++stage == kStreamStages) {
       stage = 0;
       phase ^= 1u;
     }
+  };
+  // Producer, when giving up: wait (bounded) for the copies still in flight (at most the
+  // last kStreamStages stages) so none lands in shared memory after the CTA exits.
+  auto drain = [&]() {
+    for (long long i = issued > kStreamStages ? issued - kStreamStages : 0; i < issued; ++i)
+      mbar_drain(&S.full[i % kStreamStages], static_cast<uint32_t>((i / kStreamStages) & 1), wait_ns);
   };
   const size_t row1 = static_cast<size_t>(H) * 2;  // bytes of one gate/up row
   const size_t row2 = static_cast<size_t>(F) * 2;  // bytes of one down row
@@ -872,7 +880,7 @@ __global__ void __launch_bounds__(kStreamThreads, 1) decode_stream_linear(
         }
         const UnitCoord c = unit_coord(S, u, plan.nfr, plan.r1, F, n_groups);
         const int e = G.expert[c.g];
-        if (!mbar_wait_bounded(&S.empty[stage], phase ^ 1u, status, kStatusTimeoutProducer, abort_flag)) {
+        if (!mbar_wait_bounded(&S.empty[stage], phase ^ 1u, status, kStatusTimeoutProducer, abort_flag, wait_ns)) {
           ok = false;
           break;
         }
@@ -887,7 +895,7 @@ __global__ void __launch_bounds__(kStreamThreads, 1) decode_stream_linear(
       // phase-2 weight rows do not depend on phase 1: queue the first stages now
       for (int u = u2_begin; u < u2_end && prefetched < kStreamStages && ok; ++u, ++prefetched) {
         const UnitCoord c = unit_coord(S, u, plan.nhr, plan.r2, H, n_groups);
-        if (!mbar_wait_bounded(&S.empty[stage], phase ^ 1u, status, kStatusTimeoutProducer, abort_flag)) {
+        if (!mbar_wait_bounded(&S.empty[stage], phase ^ 1u, status, kStatusTimeoutProducer, abort_flag, wait_ns)) {
           ok = false;
           break;
         }
@@ -898,11 +906,17 @@ __global__ void __launch_bounds__(kStreamThreads, 1) decode_stream_linear(
         advance();
       }
     }
-    if (!grid_barrier_bounded(barrier, gridDim.x, status, kStatusTimeoutOther, &G.flag) || *abort_flag) return;
+    if (!grid_barrier_bounded(barrier, gridDim.x, status, kStatusTimeoutOther, &G.flag, wait_ns) || *abort_flag) {
+      if (lane == 0) drain();
+      return;
+    }
     if (lane == 0 && ok) {
       for (int u = u2_begin + prefetched; u < u2_end; ++u) {
         const UnitCoord c = unit_coord(S, u, plan.nhr, plan.r2, H, n_groups);
-        if (!mbar_wait_bounded(&S.empty[stage], phase ^ 1u, status, kStatusTimeoutProducer, abort_flag)) break;
+        if (!mbar_wait_bounded(&S.empty[stage], phase ^ 1u, status, kStatusTimeoutProducer, abort_flag, wait_ns)) {
+          drain();
+          break;
+        }
         mbar_arrive_expect_tx(&S.full[stage], static_cast<uint32_t>(c.rows * row2));
         bulk_copy_g2s(ring + stage * kStreamStageBytes,
                       reinterpret_cast<const uint8_t*>(w2) + (static_cast<size_t>(G.expert[c.g]) * H + c.r0) * row2,
@@ -914,7 +928,7 @@ __global__ void __launch_bounds__(kStreamThreads, 1) decode_stream_linear(
     // ------------------------------------------------------------ consumers, phase 1
     for (int u = blockIdx.x; u < units1; u += gridDim.x) {
       const UnitCoord c = unit_coord(S, u, plan.nfr, plan.r1, F, n_groups);
-      if (!mbar_wait_bounded(&S.full[stage], phase, status, kStatusTimeoutOther, abort_flag)) {
+      if (!mbar_wait_bounded(&S.full[stage], phase, status, kStatusTimeoutOther, abort_flag, wait_ns)) {
         ok = false;
         break;
       }
@@ -962,7 +976,7 @@ __global__ void __launch_bounds__(kStreamThreads, 1) decode_stream_linear(
       advance();
     }
     DECODE_TRACE(2);
-    if (!grid_barrier_bounded(barrier, gridDim.x, status, kStatusTimeoutOther, &G.flag) || *abort_flag) return;
+    if (!grid_barrier_bounded(barrier, gridDim.x, status, kStatusTimeoutOther, &G.flag, wait_ns) || *abort_flag) return;
     DECODE_TRACE(3);
     // ------------------------------------------------------------ consumers, phase 2
     int cur_g = -1, cur_p0 = -1;
@@ -978,7 +992,7 @@ __global__ void __launch_bounds__(kStreamThreads, 1) decode_stream_linear(
         cur_g = c.g;
         cur_p0 = c.p0;
       }
-      if (!mbar_wait_bounded(&S.full[stage], phase, status, kStatusTimeoutOther, abort_flag)) break;
+      if (!mbar_wait_bounded(&S.full[stage], phase, status, kStatusTimeoutOther, abort_flag, wait_ns)) break;
       const uint8_t* st = ring + stage * kStreamStageBytes;
       for (int b = 0; b < c.nb; ++b) {
         float acc[kStreamMaxR2];
@@ -1111,13 +1125,11 @@ cudaError_t launch_decode(const DecodeArgs& a, const DecodeWorkspace& ws, cudaSt
     const size_t smem = ((sizeof(StreamShared) + 127) & ~size_t(127)) +
                         static_cast<size_t>(kStreamStages) * kStreamStageBytes + opnd;
     if (plan.r1 > 0 && plan.r2 > 0 && smem <= 220 * 1024) {
-      static bool attr_done = false;
-      if (!attr_done) {
-        if ((err = cudaFuncSetAttribute(decode_stream_linear, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                        220 * 1024)) != cudaSuccess)
-          return err;
-        attr_done = true;
-      }
+      static PerDeviceOnce smem_attr;
+      if ((err = smem_attr.run([] {
+             return cudaFuncSetAttribute(decode_stream_linear, cudaFuncAttributeMaxDynamicSharedMemorySize, 220 * 1024);
+           })) != cudaSuccess)
+        return err;
       int per_sm = 0;
       if ((err = cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, decode_stream_linear, kStreamThreads,
                                                                 smem)) != cudaSuccess)
@@ -1139,7 +1151,7 @@ cudaError_t launch_decode(const DecodeArgs& a, const DecodeWorkspace& ws, cudaSt
       cfg.numAttrs = 1;
       err = cudaLaunchKernelEx(&cfg, decode_stream_linear, a.x, a.w1, a.w2, a.indices, a.weights, a.tokens, a.topk,
                                a.experts, H, F, ws.glu, ws.partial, reinterpret_cast<unsigned*>(ws.counters),
-                               ws.status, a.out);
+                               ws.status, a.out, wait_limit_ns(kWaitLimitNs));
       if (err != cudaSuccess) return err;
       return cudaGetLastError();
     }

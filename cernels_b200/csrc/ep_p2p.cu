@@ -20,7 +20,8 @@
 // A rank starts step e+1 only after its combine of step e saw every destination's results,
 // and a destination signals results only after its GEMMs finished reading recv, so no slot
 // is overwritten while in use. Loads and stores are plain 16-byte accesses (no TMA and no
-// multicast on peer memory). Every wait gives up after kEpWaitNs and records a status.
+// multicast on peer memory). Every wait gives up after a limit (5 s unless
+// cernels_set_wait_limit_ns set another) and records a status.
 #include <cstdio>
 #include <cstring>
 
@@ -53,11 +54,11 @@ __device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
 }
 
 // Bounded wait until *flag == epoch. Returns false (and records `code`) on timeout.
-__device__ bool wait_epoch(const uint32_t* flag, uint32_t epoch, int* status, int code) {
+__device__ bool wait_epoch(const uint32_t* flag, uint32_t epoch, int* status, int code, unsigned long long limit_ns) {
   if (ld_acquire_sys(flag) == epoch) return true;
   const unsigned long long t0 = global_timer_ns();
   while (ld_acquire_sys(flag) != epoch) {
-    if (global_timer_ns() - t0 > kEpWaitNs) {
+    if (global_timer_ns() - t0 > limit_ns) {
       atomicCAS(status, 0, code);
       return false;
     }
@@ -72,6 +73,7 @@ __device__ __forceinline__ EpHeader* hdr_of(uint8_t* window, int peer) {
 struct EpGeometry {
   int rank, world, local_experts, cap, hidden;
   size_t recv_offset, back_offset;
+  unsigned long long wait_ns;  // limit of each bounded wait
 };
 
 // Marks this CTA done; the last CTA of the grid returns true (counter reset for the next launch).
@@ -139,7 +141,7 @@ __global__ void __launch_bounds__(1024) ep_segments_kernel(uint8_t* __restrict__
   }
   __syncthreads();
   if (threadIdx.x < g.world)
-    if (!wait_epoch(&hdr_of(window, threadIdx.x)->data_epoch, epoch, status, kStatusTimeoutOther)) ok = 0;
+    if (!wait_epoch(&hdr_of(window, threadIdx.x)->data_epoch, epoch, status, kStatusTimeoutOther, g.wait_ns)) ok = 0;
   __syncthreads();
   fence_proxy_async_global();  // peer-written rows are read next by TMA (async proxy)
   const int El = g.local_experts, G = g.world * El;
@@ -225,7 +227,7 @@ __global__ void __launch_bounds__(kEpThreads) ep_combine_kernel(uint8_t* __restr
   if (threadIdx.x == 0) ok = 1;
   __syncthreads();
   if (threadIdx.x < g.world)
-    if (!wait_epoch(&hdr_of(window, threadIdx.x)->result_epoch, epoch, status, kStatusTimeoutOther)) ok = 0;
+    if (!wait_epoch(&hdr_of(window, threadIdx.x)->result_epoch, epoch, status, kStatusTimeoutOther, g.wait_ns)) ok = 0;
   __syncthreads();
   const uint4* back = reinterpret_cast<const uint4*>(window + g.back_offset);
   const int vec = g.hidden / 8;
@@ -278,6 +280,13 @@ int rc_of(cudaError_t e) {
   if (e == cudaSuccess) return CERNELS_OK;
   std::fprintf(stderr, "cernels_b200 ep: CUDA error: %s\n", cudaGetErrorString(e));
   return CERNELS_E_CUDA;
+}
+
+// The geometry handed to a kernel, with the current wait limit.
+EpGeometry geo_now(const cernels_ep_ctx* c) {
+  EpGeometry g = c->geo;
+  g.wait_ns = wait_limit_ns(kEpWaitNs);
+  return g;
 }
 
 int ep_grid(int rows) {
@@ -367,7 +376,7 @@ int cernels_ep_dispatch(void* ctx, const void* x, const int32_t* perm_token, con
   if (rows > 0 && (!x || !perm_token || !offsets)) return CERNELS_E_NULL;
   if (x && (reinterpret_cast<uintptr_t>(x) & 15)) return CERNELS_E_ALIGNMENT;
   ep_dispatch_kernel<<<ep_grid(rows), kEpThreads, 0, static_cast<cudaStream_t>(stream)>>>(
-      c->d_peers, c->geo, static_cast<const uint4*>(x), perm_token, offsets, epoch, c->d_counters, c->d_status);
+      c->d_peers, geo_now(c), static_cast<const uint4*>(x), perm_token, offsets, epoch, c->d_counters, c->d_status);
   return rc_of(cudaGetLastError());
 }
 
@@ -408,7 +417,7 @@ int cernels_ep_experts(void* ctx, const cernels_moe_shape* shape, const void* ga
   off = align_up(off + rows * s.intermediate * 2, 256);
   __nv_bfloat16* down_out = reinterpret_cast<__nv_bfloat16*>(base + off);
 
-  ep_segments_kernel<<<1, 1024, 0, stream>>>(c->window, c->geo, epoch, offsets, group_rows, mtile, c->d_status);
+  ep_segments_kernel<<<1, 1024, 0, stream>>>(c->window, geo_now(c), epoch, offsets, group_rows, mtile, c->d_status);
   cudaError_t err = cudaGetLastError();
   if (err != cudaSuccess) return rc_of(err);
   const bool gptoss = s.layout == CERNELS_LAYOUT_GPTOSS;
@@ -441,7 +450,7 @@ int cernels_ep_experts(void* ctx, const cernels_moe_shape* shape, const void* ga
   if ((err = launch_grouped_gemm(gptoss ? kDownGptOss : kDownLinear, g2, sms, stream)) != cudaSuccess)
     return rc_of(err);
   ep_return_kernel<<<ep_grid(static_cast<int>(c->geo.cap)), kEpThreads, 0, stream>>>(
-      c->d_peers, c->geo, reinterpret_cast<const uint4*>(down_out), epoch, c->d_counters + 1);
+      c->d_peers, geo_now(c), reinterpret_cast<const uint4*>(down_out), epoch, c->d_counters + 1);
   return rc_of(cudaGetLastError());
 }
 
@@ -453,7 +462,7 @@ int cernels_ep_combine(void* ctx, const int32_t* inv, const float* weights, int3
   if (tokens > 0 && (!inv || !weights || !out)) return CERNELS_E_NULL;
   const int blocks = tokens > 0 ? ep_grid(tokens) : 1;
   ep_combine_kernel<<<blocks, kEpThreads, 0, static_cast<cudaStream_t>(stream)>>>(
-      c->window, c->geo, epoch, inv, weights, tokens, topk, static_cast<uint4*>(out), c->d_status);
+      c->window, geo_now(c), epoch, inv, weights, tokens, topk, static_cast<uint4*>(out), c->d_status);
   return rc_of(cudaGetLastError());
 }
 

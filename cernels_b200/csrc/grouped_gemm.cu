@@ -149,6 +149,7 @@ __global__ void __launch_bounds__(kThreads, 1)
       int stage = 0;
       uint32_t phase = 0;
       bool ok = true;
+      long long issued = 0;  // stages loaded so far
       for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x) {
         const TileCoord c = decode_tile(t, n_tiles, s_mt, experts);
         const int row0 = args.offsets[c.expert] + c.m_tile * BM;
@@ -156,7 +157,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const CUtensorMap* bmap = extra ? &tmap_b_extra : &tmap_b;
         const int we = extra ? 0 : c.expert % args.weight_experts;  // weight slab of this row group
         for (int kb = 0; kb < k_blocks; ++kb) {
-          if (!mbar_wait_bounded(&empty_bar[stage], phase ^ 1u, args.status, kStatusTimeoutProducer, abort_flag)) {
+          if (!mbar_wait_bounded(&empty_bar[stage], phase ^ 1u, args.status, kStatusTimeoutProducer, abort_flag, args.wait_ns)) {
             ok = false;
             break;
           }
@@ -179,11 +180,18 @@ __global__ void __launch_bounds__(kThreads, 1)
               tma_load_3d(b_dst + j * kBoxBytes, bmap, &full_bar[stage], c.n_tile * BN + 64 * j, kb * BK,
                           we, kCacheEvictNormal);
           }
+          ++issued;
           if (++stage == kStages) {
             stage = 0;
             phase ^= 1u;
           }
         }
+      }
+      if (!ok) {
+        // Giving up: let the loads still in flight (at most the last kStages) land before
+        // this CTA exits, so none writes shared memory the CTA no longer owns.
+        for (long long i = issued > kStages ? issued - kStages : 0; i < issued; ++i)
+          mbar_drain(&full_bar[i % kStages], static_cast<uint32_t>((i / kStages) & 1), args.wait_ns);
       }
     }
   } else if (warp == 1) {
@@ -197,11 +205,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x, ++local) {
         const int acc = local & 1;
         const uint32_t acc_phase = (local >> 1) & 1;
-        if (!mbar_wait_bounded(&tempty_bar[acc], acc_phase ^ 1u, args.status, kStatusTimeoutMma, abort_flag)) break;
+        if (!mbar_wait_bounded(&tempty_bar[acc], acc_phase ^ 1u, args.status, kStatusTimeoutMma, abort_flag, args.wait_ns)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + static_cast<uint32_t>(acc * kAccStride);
         for (int kb = 0; kb < k_blocks; ++kb) {
-          if (!mbar_wait_bounded(&full_bar[stage], phase, args.status, kStatusTimeoutMma, abort_flag)) {
+          if (!mbar_wait_bounded(&full_bar[stage], phase, args.status, kStatusTimeoutMma, abort_flag, args.wait_ns)) {
             ok = false;
             break;
           }
@@ -235,7 +243,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     for (int t = blockIdx.x; t < total_tiles; t += gridDim.x, ++local) {
       const int acc = local & 1;
       const uint32_t acc_phase = (local >> 1) & 1;
-      if (!mbar_wait_bounded(&tfull_bar[acc], acc_phase, args.status, kStatusTimeoutEpilogue, abort_flag)) break;
+      if (!mbar_wait_bounded(&tfull_bar[acc], acc_phase, args.status, kStatusTimeoutEpilogue, abort_flag, args.wait_ns)) break;
       tc_fence_after();
       const TileCoord c = decode_tile(t, n_tiles, s_mt, experts);
       const int e = (args.b_extra != nullptr && c.expert == args.extra_group) ? 0 : c.expert % args.weight_experts;
@@ -383,20 +391,20 @@ cudaError_t launch_mode(const GroupedGemmArgs& args, int num_sms, cudaStream_t s
     map_b_extra = map_b;
   }
   const size_t smem = smem_fixed(BN) + 1024 + static_cast<size_t>(args.experts + 1) * sizeof(int);
-  static bool attr_set = false;
-  if (!attr_set) {
-    cudaError_t err =
-        cudaFuncSetAttribute(grouped_gemm_kernel<kMode, BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             static_cast<int>(smem_fixed(BN) + 1024 + (kMaxExperts + 1) * sizeof(int)));
-    if (err != cudaSuccess) return err;
-    attr_set = true;
-  }
+  static PerDeviceOnce attr;
+  cudaError_t err = attr.run([] {
+    return cudaFuncSetAttribute(grouped_gemm_kernel<kMode, BN>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                static_cast<int>(smem_fixed(BN) + 1024 + (kMaxExperts + 1) * sizeof(int)));
+  });
+  if (err != cudaSuccess) return err;
   const int n_tiles = n_tiles_for(kMode, args.n, BN);
   const long long max_mtiles = (static_cast<long long>(args.rows) + BM - 1) / BM + args.experts;
   const long long max_tiles = max_mtiles * n_tiles;
   const int grid = static_cast<int>(max_tiles < num_sms ? max_tiles : num_sms);
   if (grid <= 0) return cudaSuccess;
-  grouped_gemm_kernel<kMode, BN><<<grid, kThreads, smem, stream>>>(map_a, map_b, map_b_extra, args);
+  GroupedGemmArgs a = args;
+  a.wait_ns = wait_limit_ns(kWaitLimitNs);
+  grouped_gemm_kernel<kMode, BN><<<grid, kThreads, smem, stream>>>(map_a, map_b, map_b_extra, a);
   return cudaGetLastError();
 }
 

@@ -5,6 +5,7 @@
 #include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
+#include <atomic>
 #include <cstddef>
 #include <cstdint>
 
@@ -27,6 +28,28 @@ constexpr int kBlockM = 128;
 constexpr int kDecodeMaxPairs = 1024;
 
 inline size_t align_up(size_t v, size_t a) { return (v + a - 1) / a * a; }
+
+// Limit of the bounded waits inside kernels, in ns: `default_ns` unless
+// cernels_set_wait_limit_ns() set one. Read by every launcher and passed as an argument.
+unsigned long long wait_limit_ns(unsigned long long default_ns);
+
+// Runs `set` (a cudaFuncSetAttribute call) once per device: kernel attributes belong to a
+// device context, so a process that drives several GPUs needs them on each.
+struct PerDeviceOnce {
+  std::atomic<unsigned long long> done{0};
+  template <class F>
+  cudaError_t run(F&& set) {
+    int dev = 0;
+    cudaError_t err = cudaGetDevice(&dev);
+    if (err != cudaSuccess) return err;
+    if (dev < 0 || dev >= 64) return set();
+    const unsigned long long bit = 1ull << dev;
+    if (done.load(std::memory_order_acquire) & bit) return cudaSuccess;
+    err = set();  // two host threads may both get here: setting an attribute twice is harmless
+    if (err == cudaSuccess) done.fetch_or(bit, std::memory_order_acq_rel);
+    return err;
+  }
+};
 
 // Device pointers carved out of one caller-provided workspace allocation.
 struct PrefillWorkspace {
@@ -91,6 +114,7 @@ struct GroupedGemmArgs {
   int n;                       // columns of the weight product (2F or H)
   int out_cols;                // F for gate/up, H for down
   int weight_experts;          // experts in the weight tensors; row group g uses expert g % weight_experts
+  unsigned long long wait_ns;  // limit of each bounded mbarrier wait
   const int* group_rows;       // optional [groups]: rows of group g (default offsets[g+1] - offsets[g])
   // Optional always-on extra group (a shared expert): group `extra_group` takes its weights
   // from b_extra (one slab, same layout as b) instead of b. Unused when b_extra is null.
@@ -126,5 +150,9 @@ cudaError_t launch_router_topk(const void* logits, int bf16, int tokens, int exp
                                int shared_gate, int32_t* idx, float* w, cudaStream_t stream);
 
 int device_sm_count();
+
+// Device address of the static decode scratch of cernels_moe_experts_decode_noalloc on the
+// current device (looked up on first use per device). Returns a CERNELS_* code.
+int noalloc_scratch(void** out);
 
 }  // namespace cernels

@@ -20,7 +20,8 @@ enum DeviceStatus : int {
   kStatusTimeoutOther = 4,
 };
 
-// A wait gives up after this many nanoseconds of %globaltimer.
+// Default limit of a bounded wait, in nanoseconds of %globaltimer. Launchers pass the
+// limit to the kernels as an argument (cernels_set_wait_limit_ns changes it at run time).
 constexpr unsigned long long kWaitLimitNs = 2000000000ull;
 
 __device__ __forceinline__ unsigned long long global_timer_ns() {
@@ -74,10 +75,10 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 }
 
 // Waits for the phase with the given parity. Returns false (after recording
-// `code` in *status and raising *abort_flag) when the wall-clock limit passes
+// `code` in *status and raising *abort_flag) when `limit_ns` of wall-clock time pass
 // or another role of the same CTA has already aborted.
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, int* status, int code,
-                                                  volatile int* abort_flag) {
+                                                  volatile int* abort_flag, unsigned long long limit_ns) {
   if (mbar_try_wait(bar, parity)) return true;
   const unsigned long long t0 = global_timer_ns();
   uint32_t spins = 0;
@@ -85,13 +86,22 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
     if (mbar_try_wait(bar, parity)) return true;
     if ((++spins & 255u) == 0) {
       if (*abort_flag) return false;
-      if (global_timer_ns() - t0 > kWaitLimitNs) {
+      if (global_timer_ns() - t0 > limit_ns) {
         if (status) atomicCAS(status, 0, code);
         *abort_flag = 1;
         return false;
       }
     }
   }
+}
+
+// Waits (bounded, ignoring any abort flag) until the phase with the given parity of
+// `bar` completed. Used on the way out of a kernel that gives up, so that no bulk or
+// TMA copy still writes this CTA's shared memory after it exits.
+__device__ __forceinline__ void mbar_drain(uint64_t* bar, uint32_t parity, unsigned long long limit_ns) {
+  const unsigned long long t0 = global_timer_ns();
+  while (!mbar_try_wait(bar, parity))
+    if (global_timer_ns() - t0 > limit_ns) return;
 }
 
 // ---------------------------------------------------------------- TMA

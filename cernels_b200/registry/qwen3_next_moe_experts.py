@@ -76,6 +76,16 @@ def fused_shared_supported(block) -> bool:
     return FUSE_SHARED and se.gate_proj.weight.shape[0] == block.experts.gate_up_proj.shape[1] // 2
 
 
+def route_debug(xf, block):
+    """The routing kernel() uses when the shared expert is fused: returns (logits [T, pad8(E + 1)],
+    ids [T, k + 1] int32, weights [T, k + 1] fp32), the last column being (E, sigmoid(gate))."""
+    with torch.no_grad():
+        logits = torch.nn.functional.linear(xf, _router_and_gate(block))
+        idx, w = ops.router_topk(logits, int(block.gate.top_k), ops.ROUTER_SOFTMAX_TOPK,
+                                 bool(block.gate.norm_topk_prob), shared_gate=int(block.experts.gate_up_proj.shape[0]))
+    return logits, idx, w
+
+
 def kernel(x, block):
     if block is None:
         raise RuntimeError("block module not available (meta device)")

@@ -60,6 +60,13 @@ const char* cernels_error_string(int code);
 /* Library version as MAJOR*10000 + MINOR*100 + PATCH. */
 int cernels_version(void);
 
+/* Limit, in nanoseconds, after which every bounded wait inside this library's kernels (an
+ * mbarrier of a TMA / MMA pipeline, a grid barrier, a peer rank's flag) gives up, records a
+ * nonzero status word and lets the kernel return. 0 restores the defaults (2 s for waits
+ * inside one GPU, 5 s for waits on peer ranks). Applies to launches made after the call, from
+ * any host thread. No counterpart in the reference (its kernels never wait). */
+int cernels_set_wait_limit_ns(uint64_t ns);
+
 /* Workspace bytes needed by cernels_moe_experts (decode == 0) or
  * cernels_moe_experts_decode (decode != 0) for this shape. */
 int cernels_moe_workspace_bytes(const cernels_moe_shape* shape, int decode, size_t* bytes);
@@ -191,7 +198,7 @@ int cernels_moe_experts_decode_noalloc(const cernels_moe_shape* shape, const voi
  *   cernels_ep_combine   waits for all results, out[t] = bf16(sum_j w[t,j] * row[inv[t,j]])
  * offsets/perm_token/inv come from cernels_moe_route over the GLOBAL expert ids (experts are
  * sharded contiguously: rank r owns [r*El, (r+1)*El)). Waits inside the kernels give up after
- * 5 s and record a nonzero status (cernels_ep_status). */
+ * 5 s (see cernels_set_wait_limit_ns) and record a nonzero status (cernels_ep_status). */
 #define CERNELS_EP_HANDLE_BYTES 64
 int cernels_ep_create(int32_t rank, int32_t world, int32_t hidden, int32_t local_experts, int32_t max_rows,
                       void** ctx, void* ipc_handle_out);
@@ -208,7 +215,9 @@ int cernels_ep_combine(void* ctx, const int32_t* inv, const float* weights, int3
 int cernels_ep_status(void* ctx, int* status);
 
 /* Device status word of the last call that used this workspace (0 = ok; nonzero when a
- * bounded wait inside a kernel gave up). Reads device memory: synchronises `stream`. */
+ * bounded wait inside a kernel gave up). Reads device memory: synchronises `stream`.
+ * With decode != 0 and workspace == NULL it reads the status word of the last
+ * cernels_moe_experts_decode_noalloc call on the current device. */
 int cernels_workspace_status(const cernels_moe_shape* shape, int decode, const void* workspace, int* status,
                              void* stream);
 

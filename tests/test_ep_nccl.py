@@ -1,8 +1,8 @@
 """GPU: expert parallelism over NCCL on every visible GPU (skipped with fewer than 2).
 
-Each rank runs the EP forward on its token shard; its rows must match the single-GPU
-operator on the full batch (same kernels, so only bf16 rounding order of the combine may
-differ — the parity tolerance applies).
+Each rank runs the EP forward on its token shard. Its rows must match (1) the fp32 CPU
+oracle on a seeded sample of 64 of its tokens, routed by the same router call the EP step
+makes, and (2) the single-GPU operator on the full batch. The parity tolerance applies.
 """
 
 import os
@@ -54,6 +54,22 @@ def _worker(rank, world, port, cfg_name, tokens, transport, q):
         torch.cuda.synchronize()
         err = max(O.rel_err(out.float().cpu().numpy(), full[shard].float().cpu().numpy()),
                   O.rel_err(out2.float().cpu().numpy(), full[shard].float().cpu().numpy()))
+        # against the oracle: a seeded sample of this rank's tokens
+        xs = case.x[shard].contiguous()
+        with torch.no_grad():
+            idx, w = moe.router(xs)
+        n = xs.shape[0]
+        sample = np.sort(np.random.default_rng(rank).choice(n, min(64, n), replace=False))
+        xn = xs.float().cpu().numpy()
+        ref = O.moe_experts(xn, case.w1.float().cpu().numpy(), case.w2.float().cpu().numpy(), idx.cpu().numpy(),
+                            w.float().cpu().numpy(), cfg.layout,
+                            None if case.b1 is None else case.b1.cpu().numpy(),
+                            None if case.b2 is None else case.b2.cpu().numpy(), token_subset=sample)[sample]
+        if case.shared is not None:
+            sh = {k_: v.float().cpu().numpy() for k_, v in case.shared.items()}
+            ref = ref + O.shared_expert(xn[sample], sh["gate_proj"], sh["up_proj"], sh["down_proj"], sh["gate"])
+        err = max(err, O.rel_err(out.float().cpu().numpy()[sample], ref),
+                  O.rel_err(out2.float().cpu().numpy()[sample], ref))
         if transport == "p2p":
             assert moe._p2p is not None and moe._p2p.status() == 0
         q.put((rank, err))

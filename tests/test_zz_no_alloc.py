@@ -3,8 +3,12 @@
 It exists for callers that cannot allocate device memory themselves — runtimes that
 forbid cudaMalloc or plan every device byte at start-up — and takes its scratch from a
 static device array inside the library. This file checks, through the C ABI, that two
-calls in a row give the same result as the workspace-based decode entry point, within the
-parity tolerance used by the other GPU tests. It is named to be collected last.
+calls in a row give the same result as the workspace-based decode entry point (the same
+deterministic kernels, so the bits must match; the parity tolerance used by the other GPU
+tests is checked too), that the status word the no-alloc call leaves behind reads zero, and
+that every decode kernel family runs on the static scratch: the cooperative streaming
+kernel (a few (token, slot) pairs), the two-kernel LINEAR path and the split-K GPTOSS path.
+It is named to be collected last.
 """
 
 import ctypes
@@ -42,8 +46,9 @@ def _ptr(t):
     return None if t is None else t.data_ptr()
 
 
-@pytest.mark.parametrize("layout,dims", [(_lib.LAYOUT_LINEAR, (8, 2048, 64, 1408, 6)),
-                                         (_lib.LAYOUT_GPTOSS, (4, 2880, 32, 2880, 4))])
+@pytest.mark.parametrize("layout,dims", [(_lib.LAYOUT_LINEAR, (1, 2048, 64, 1408, 6)),   # streaming kernel
+                                         (_lib.LAYOUT_LINEAR, (8, 2048, 64, 1408, 6)),   # two-kernel path
+                                         (_lib.LAYOUT_GPTOSS, (4, 2880, 32, 2880, 4))])  # split-K GPTOSS
 def test_noalloc_decode_matches_workspace_decode(layout, dims):
     T, H, E, F, k = dims
     lib = _lib.load()
@@ -68,6 +73,10 @@ def test_noalloc_decode_matches_workspace_decode(layout, dims):
         err = O.rel_err(out.float().cpu().numpy(), ref_out.float().cpu().numpy())
         assert np.isfinite(out.float().cpu().numpy()).all()
         assert err <= TOL, f"call {seed}: rel err {err:.3e}"
+        assert torch.equal(out, ref_out), f"call {seed}: differs from the workspace decode"
+        status = ctypes.c_int(-1)
+        assert lib.cernels_workspace_status(ctypes.byref(shape), 1, None, ctypes.byref(status), stream) == 0
+        assert status.value == 0
         outs.append(out)
     assert not torch.equal(outs[0], outs[1])  # the second call really recomputed
 
