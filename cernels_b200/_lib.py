@@ -49,6 +49,8 @@ PROTOTYPES = {
                                                      ctypes.POINTER(ctypes.c_float)]),
     "cernels_moe_experts_decode_noalloc": (ctypes.c_int, [_SHAPE_P, _VP, _VP, _VP, _VP, _VP, _VP, _VP, _VP, _VP]),
     "cernels_moe_grouped_experts": (ctypes.c_int, [_SHAPE_P, _I32, _VP, _VP, _VP, _VP, _VP, _VP, _VP, _VP, _SZ, _VP]),
+    "cernels_router": (ctypes.c_int, [_VP, _I32, _I32, _VP, _I32, _VP, _I32, _I32, _I32, _I32, _I32, _VP, _VP, _VP,
+                                      _VP]),
     "cernels_router_topk": (ctypes.c_int, [_VP, _I32, _I32, _I32, _I32, _I32, _I32, _I32, _VP, _VP, _VP]),
     "cernels_moe_experts_shared": (ctypes.c_int, [_SHAPE_P, _VP, _VP, _VP, _VP, _VP, _VP, _VP, _VP, _VP, _SZ, _VP]),
     "cernels_ep_create": (ctypes.c_int, [_I32, _I32, _I32, _I32, _I32, ctypes.POINTER(_VP), _VP]),

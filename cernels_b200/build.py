@@ -18,7 +18,7 @@ REPO_DIR = PKG_DIR.parent
 CSRC = PKG_DIR / "csrc"
 OUT_DIR = PKG_DIR / "_C"
 LIB_NAME = "libcernels_b200.so"
-SOURCES = ["capi.cu", "route.cu", "permute.cu", "grouped_gemm.cu", "decode.cu", "capi_noalloc.cu", "router.cu", "ep_p2p.cu"]
+SOURCES = ["capi.cu", "route.cu", "permute.cu", "grouped_gemm.cu", "decode.cu", "capi_noalloc.cu", "router.cu", "router_gemm.cu", "ep_p2p.cu"]
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

@@ -406,6 +406,24 @@ int cernels_router_topk(const void* logits, int32_t logits_bf16, int32_t tokens,
                                     shared_gate != 0, indices, weights, static_cast<cudaStream_t>(stream)));
 }
 
+int cernels_router(const void* x, int32_t tokens, int32_t hidden, const void* router_weight, int32_t weight_rows,
+                   const void* router_bias, int32_t experts, int32_t topk, int32_t mode, int32_t renorm,
+                   int32_t shared_gate, int32_t* indices, float* weights, void* logits_out, void* stream) {
+  if (tokens < 0 || hidden <= 0 || experts <= 0 || topk <= 0 || topk > 16 || topk > experts)
+    return CERNELS_E_INVALID_SHAPE;
+  if (mode != CERNELS_ROUTER_TOPK_SOFTMAX && mode != CERNELS_ROUTER_SOFTMAX_TOPK) return CERNELS_E_INVALID_SHAPE;
+  const int cols = experts + (shared_gate ? 1 : 0);
+  if (weight_rows < cols || cols > 8 * 256) return CERNELS_E_INVALID_SHAPE;
+  if (hidden % 8) return CERNELS_E_ALIGNMENT;
+  if (tokens == 0) return CERNELS_OK;
+  if (!x || !router_weight || !indices || !weights) return CERNELS_E_NULL;
+  if (!aligned16(x) || !aligned16(router_weight)) return CERNELS_E_ALIGNMENT;
+  if (const int rc = check_device()) return rc;
+  return cuda_rc(launch_router_gemm(x, tokens, hidden, router_weight, weight_rows, router_bias, experts, topk, mode,
+                                    renorm != 0, shared_gate != 0, indices, weights, logits_out, nullptr,
+                                    static_cast<cudaStream_t>(stream)));
+}
+
 int cernels_moe_route(const cernels_moe_shape* shape, const int32_t* indices, const float* weights,
                       int32_t* offsets, int32_t* perm_token, float* perm_weight, int32_t* inv, void* workspace,
                       size_t workspace_bytes, void* stream_ptr) {

@@ -359,6 +359,15 @@ bool encode_map(CUtensorMap* map, const void* ptr, int rank, const uint64_t* dim
   return r == CUDA_SUCCESS;
 }
 
+}  // namespace
+
+bool encode_bf16_map(CUtensorMap* map, const void* ptr, int rank, const uint64_t* dims, const uint64_t* byte_strides,
+                     const uint32_t* box) {
+  return encode_map(map, ptr, rank, dims, byte_strides, box);
+}
+
+namespace {
+
 template <int kMode, int BN>
 cudaError_t launch_mode(const GroupedGemmArgs& args, int num_sms, cudaStream_t stream) {
   CUtensorMap map_a, map_b;

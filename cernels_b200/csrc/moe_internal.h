@@ -151,6 +151,20 @@ cudaError_t launch_router_topk(const void* logits, int bf16, int tokens, int exp
 
 int device_sm_count();
 
+// Tiled bf16 TMA map with 128-byte swizzle (grouped_gemm.cu).
+bool encode_bf16_map(CUtensorMap* map, const void* ptr, int rank, const uint64_t* dims, const uint64_t* byte_strides,
+                     const uint32_t* box);
+
+// Fused router GEMM + top-k tail (router_gemm.cu): column split of the logits over a cluster
+// of nc CTAs (bn columns each), 128-token tiles.
+struct RouterPlan {
+  int nc, bn, kmax, tmem_cols, m_tiles;
+};
+RouterPlan router_plan(int tokens, int experts, int weight_rows, int gate, int topk);
+cudaError_t launch_router_gemm(const void* x, int tokens, int hidden, const void* w, int weight_rows,
+                               const void* bias, int experts, int topk, int mode, int renorm, int gate,
+                               int32_t* indices, float* weights, void* logits, int* status, cudaStream_t stream);
+
 // Device address of the static decode scratch of cernels_moe_experts_decode_noalloc on the
 // current device (looked up on first use per device). Returns a CERNELS_* code.
 int noalloc_scratch(void** out);

@@ -315,6 +315,37 @@ def router_topk(logits: torch.Tensor, topk: int, mode: int, renorm: bool = False
     return idx, w
 
 
+def router(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None, experts: int, topk: int, mode: int,
+           renorm: bool = False, shared_gate: bool = False, return_logits: bool = False):
+    """Fused router (cernels_router): logits = x weight^T (+ bias) on the tensor cores with the
+    top-k / softmax tail in the same kernel; returns int32 ids and fp32 weights [T, topk (+1)]
+    (and, with return_logits, the bf16 logits [T, weight.shape[0]] the selection used; only the
+    first experts (+1) columns are written). weight: [rows >= experts (+1), H] bf16; with
+    shared_gate, row `experts` is a shared expert's gate and an (experts, sigmoid(gate)) slot is
+    appended to every token."""
+    _check(x.is_cuda and x.dim() == 2 and x.dtype == torch.bfloat16, "x must be a [T, H] bf16 CUDA tensor")
+    _check(weight.is_cuda and weight.dim() == 2 and weight.dtype == torch.bfloat16 and weight.shape[1] == x.shape[1],
+           "router weight must be [rows, H] bf16")
+    _check(bias is None or (bias.dtype == torch.bfloat16 and bias.numel() >= experts), "router bias must be bf16 [E]")
+    x = x.contiguous()
+    weight = weight.contiguous()
+    bias = None if bias is None else bias.contiguous()
+    T = x.shape[0]
+    cols = topk + int(bool(shared_gate))
+    idx = torch.empty(T, cols, dtype=torch.int32, device=x.device)
+    w = torch.empty(T, cols, dtype=torch.float32, device=x.device)
+    logits = torch.zeros(T, weight.shape[0], dtype=torch.bfloat16, device=x.device) if return_logits else None
+    with torch.cuda.device(x.device):
+        rc = _lib.load().cernels_router(x.data_ptr(), T, x.shape[1], weight.data_ptr(), weight.shape[0], _ptr(bias),
+                                        int(experts), int(topk), int(mode), int(bool(renorm)), int(bool(shared_gate)),
+                                        idx.data_ptr(), w.data_ptr(), _ptr(logits), _stream_handle(x.device))
+    _lib.check(rc, "cernels_router")
+    return (idx, w, logits) if return_logits else (idx, w)
+
+
+ROUTER_MAX_TOPK = 16
+
+
 def gather_rows(x: torch.Tensor, perm_token: torch.Tensor, rows: int | None = None) -> torch.Tensor:
     """rows_out[i] = x[perm_token[i]] for i < rows (bf16 [rows, H])."""
     _check(x.is_cuda and x.dtype == torch.bfloat16 and x.is_contiguous() and x.dim() == 2, "x must be [T, H] bf16")

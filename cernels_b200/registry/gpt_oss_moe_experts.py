@@ -1,8 +1,8 @@
 """gpt_oss_moe_experts loader — drop-in for src/kops/registry/gpt_oss_moe_experts.py.
 
 ``kernel(x, mlp)`` takes hidden states [B, S, H] and a GptOssMLP. The router runs in the
-timed path, as in the reference loader: its linear in cuBLAS (torch), its top-k + softmax in
-one kernel (cernels_router_topk); the CUDA op does routing, both grouped GEMMs (with biases) and the
+timed path, as in the reference loader: its linear, top-k and softmax in one tensor-core
+kernel (cernels_router); the CUDA op does routing, both grouped GEMMs (with biases) and the
 clamped interleaved SwiGLU. Weights are consumed in place in the transformers layout
 ([E, H, 2F] interleaved gate/up, [E, F, H]); only the fp32 bias casts are cached on the
 module, as the reference does (its ``_kops_weights``).
@@ -23,10 +23,16 @@ def _weights(experts):
 
 
 def route(xf, mlp):
-    """transformers GptOssTopKRouter: logits = x W^T + b (cuBLAS via torch), then top-k and the
-    softmax over the k logits in one kernel (int32 ids, fp32 weights)."""
-    logits = torch.nn.functional.linear(xf, mlp.router.weight, mlp.router.bias)
-    return ops.router_topk(logits, int(mlp.router.top_k), ops.ROUTER_TOPK_SOFTMAX)
+    """transformers GptOssTopKRouter in one kernel (cernels_router): logits = x W^T + b on the
+    tensor cores, rounded to bf16, top-k and the softmax over the k logits in its epilogue
+    (int32 ids, fp32 weights)."""
+    r = mlp.router
+    k = int(r.top_k)
+    if k > ops.ROUTER_MAX_TOPK:  # beyond the fused kernel's limit: linear, then the tail kernel
+        logits = torch.nn.functional.linear(xf, r.weight, r.bias)
+        return ops.router_topk(logits, k, ops.ROUTER_TOPK_SOFTMAX)
+    return ops.router(xf, r.weight.data, None if r.bias is None else r.bias.data, int(r.weight.shape[0]), k,
+                      ops.ROUTER_TOPK_SOFTMAX)
 
 
 def kernel(x, mlp):

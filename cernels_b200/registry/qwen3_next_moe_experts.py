@@ -2,14 +2,14 @@
 
 ``kernel(x, block)`` takes the raw hidden states [B, S, H] and a
 Qwen3NextSparseMoeBlock. As in the reference loader, the router runs in the timed path:
-its linear in cuBLAS (torch), softmax + top-k + renorm in one kernel (cernels_router_topk); the routed experts run in
-the CUDA op; the always-on shared expert ``sigmoid(shared_expert_gate(x)) *
+its linear, softmax, top-k and renorm in one tensor-core kernel (cernels_router); the routed
+experts run in the CUDA op; the always-on shared expert ``sigmoid(shared_expert_gate(x)) *
 shared_expert(x)`` runs through the same CUDA grouped-GEMM path as a one-expert,
 one-slot problem whose router weight is the sigmoid gate (its gate/up weights are
 concatenated once into the [1, 2Fs, H] layout and cached on the block). When the shared
 intermediate size equals the routed one (Qwen3-Next: 512), ``kernel`` instead folds the shared
-expert into the routed call: one router GEMM over [W_router; g_shared], one router-tail kernel
-that appends a (E, sigmoid(gate)) slot to every token, and the shared expert as an always-on
+expert into the routed call: one router kernel over [W_router; g_shared] that appends a
+(E, sigmoid(gate)) slot to every token, and the shared expert as an always-on
 group of the same grouped GEMMs (cernels_moe_experts_shared).
 """
 
@@ -45,10 +45,16 @@ def shared_expert(xf: torch.Tensor, block) -> torch.Tensor:
 
 
 def route(xf, block):
-    """transformers Qwen3NextTopKRouter: logits = x W^T (cuBLAS via torch), then fp32 softmax,
-    top-k and renormalisation in one kernel (int32 ids, fp32 weights)."""
-    logits = torch.nn.functional.linear(xf, block.gate.weight)
-    return ops.router_topk(logits, int(block.gate.top_k), ops.ROUTER_SOFTMAX_TOPK, bool(block.gate.norm_topk_prob))
+    """transformers Qwen3NextTopKRouter in one kernel (cernels_router): logits = x W^T on the
+    tensor cores, rounded to bf16, then fp32 softmax, top-k and renormalisation in its epilogue
+    (int32 ids, fp32 weights)."""
+    k = int(block.gate.top_k)
+    renorm = bool(block.gate.norm_topk_prob)
+    if k > ops.ROUTER_MAX_TOPK:
+        logits = torch.nn.functional.linear(xf, block.gate.weight)
+        return ops.router_topk(logits, k, ops.ROUTER_SOFTMAX_TOPK, renorm)
+    return ops.router(xf, block.gate.weight.data, None, int(block.gate.weight.shape[0]), k, ops.ROUTER_SOFTMAX_TOPK,
+                      renorm)
 
 
 def _router_and_gate(block):
@@ -76,14 +82,26 @@ def fused_shared_supported(block) -> bool:
     return FUSE_SHARED and se.gate_proj.weight.shape[0] == block.experts.gate_up_proj.shape[1] // 2
 
 
+def _fused_route(xf, block, return_logits=False):
+    """Router + shared-expert gate in one kernel: ids / weights [T, k + 1], the last column
+    (E, sigmoid(gate)); with return_logits also the bf16 logits [T, pad8(E + 1)]."""
+    E = int(block.experts.gate_up_proj.shape[0])
+    k = int(block.gate.top_k)
+    renorm = bool(block.gate.norm_topk_prob)
+    wg = _router_and_gate(block)
+    if k > ops.ROUTER_MAX_TOPK:
+        logits = torch.nn.functional.linear(xf, wg)
+        idx, w = ops.router_topk(logits, k, ops.ROUTER_SOFTMAX_TOPK, renorm, shared_gate=E)
+        return (logits, idx, w) if return_logits else (idx, w)
+    r = ops.router(xf, wg, None, E, k, ops.ROUTER_SOFTMAX_TOPK, renorm, shared_gate=True, return_logits=return_logits)
+    return (r[2], r[0], r[1]) if return_logits else r
+
+
 def route_debug(xf, block):
     """The routing kernel() uses when the shared expert is fused: returns (logits [T, pad8(E + 1)],
     ids [T, k + 1] int32, weights [T, k + 1] fp32), the last column being (E, sigmoid(gate))."""
     with torch.no_grad():
-        logits = torch.nn.functional.linear(xf, _router_and_gate(block))
-        idx, w = ops.router_topk(logits, int(block.gate.top_k), ops.ROUTER_SOFTMAX_TOPK,
-                                 bool(block.gate.norm_topk_prob), shared_gate=int(block.experts.gate_up_proj.shape[0]))
-    return logits, idx, w
+        return _fused_route(xf, block, return_logits=True)
 
 
 def kernel(x, block):
@@ -97,9 +115,7 @@ def kernel(x, block):
         if fused_shared_supported(block):
             # router + shared gate in one GEMM, top-k + renorm + sigmoid gate in one kernel, and
             # the shared expert as an always-on group of the same grouped GEMMs
-            logits = torch.nn.functional.linear(xf, _router_and_gate(block))
-            idx, w = ops.router_topk(logits, k, ops.ROUTER_SOFTMAX_TOPK, bool(block.gate.norm_topk_prob),
-                                     shared_gate=int(e.gate_up_proj.shape[0]))
+            idx, w = _fused_route(xf, block)
             sw1, sw2 = _shared_weights(block)
             out = ops.run_experts_shared(xf, e.gate_up_proj.data.contiguous(), e.down_proj.data.contiguous(), sw1,
                                          sw2, idx, w, k)

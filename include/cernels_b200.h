@@ -149,6 +149,20 @@ int cernels_router_topk(const void* logits, int32_t logits_bf16, int32_t tokens,
  * indices / weights get topk + 1 columns, the last = (E, sigmoid(gate logit)) — the input of
  * cernels_moe_experts_shared. */
 
+/* Fused router: logits = x router_weight^T (+ router_bias) computed on the tcgen05 tensor
+ * cores, rounded to bf16 (the dtype the transformers linear produces), and the router tail of
+ * cernels_router_topk (same modes, same tie rule) applied in the same kernel, so the logits
+ * never reach global memory. x [T, H] bf16; router_weight [weight_rows, H] bf16 with
+ * weight_rows >= experts (+ 1 with shared_gate, whose row `experts` is the shared expert's gate);
+ * router_bias [experts] bf16 or NULL. Writes indices / weights [T, topk (+ 1)] as
+ * cernels_router_topk does; logits_out, if not NULL, receives the bf16 logits [T, weight_rows]
+ * (columns 0..experts (+ 1) - 1 only; for tests). topk <= 16, experts (+ 1) <= 2048.
+ * Replaces the router linear + topk + softmax + casts of the reference loaders
+ * (src/kops/registry/gpt_oss_moe_experts.py:35, src/kops/registry/qwen3_next_moe_experts.py:28). */
+int cernels_router(const void* x, int32_t tokens, int32_t hidden, const void* router_weight, int32_t weight_rows,
+                   const void* router_bias, int32_t experts, int32_t topk, int32_t mode, int32_t renorm,
+                   int32_t shared_gate, int32_t* indices, float* weights, void* logits_out, void* stream);
+
 /* Gather: rows_out[i, :] = x[perm_token[i], :] for i < rows ([rows, H] bf16). Replaces
  * gather_kernel (src/kops/cohere2_moe_experts/csrc/cohere2_moe_experts.cu:58-65). Used by
  * expert parallelism to build the dispatch send buffer in routed order. */
