@@ -519,13 +519,14 @@ def test_fused_router_matches_oracle(mode, T, H, E, k, renorm, gate, bias):
     if b is not None:
         ref[:, :E] += b.float().numpy()
     step = np.maximum(np.abs(ref), 1e-30) * 2.0 ** -7
-    assert np.all(np.abs(lg - ref) <= step + 1e-6)
+    assert np.all(np.abs(lg - ref) <= step + 1e-4)  # absolute slack: cancellation near zero
     assert np.mean(lg == _bf16_np(ref)) > 0.99
     r_idx, r_w = O.router_tail(lg[:, :E], k, mode, renorm)
     assert np.array_equal(idx[:, :k].cpu().numpy(), r_idx)
-    if mode == 0:
-        r_w = _bf16_np(r_w)
-    assert np.allclose(w[:, :k].cpu().numpy(), r_w, atol=1e-6, rtol=1e-5)
+    if mode == 0:  # gpt-oss weights are rounded to bf16: one bf16 step apart at a rounding boundary
+        assert np.allclose(w[:, :k].cpu().numpy(), _bf16_np(r_w), atol=1e-6, rtol=2.0 ** -8)
+    else:
+        assert np.allclose(w[:, :k].cpu().numpy(), r_w, atol=1e-6, rtol=1e-5)
     if gate:
         assert np.all(idx[:, k].cpu().numpy() == E)
         assert np.allclose(w[:, k].cpu().numpy(), 1.0 / (1.0 + np.exp(-lg[:, E])), atol=1e-6, rtol=1e-5)
