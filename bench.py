@@ -177,7 +177,9 @@ def make_step(cfg, case, kind, module, world, rank):
         planner = ep.ExpertParallelMoe.from_module(kind, module, rank, world)
         shard = ep.token_shard(cfg.tokens, rank, world)
         x = case.x[shard].contiguous()
-        return (lambda xx: planner.forward(xx)), [x], planner.launches_per_step
+        step = lambda xx: planner.forward(xx)  # noqa: E731
+        step.planner = planner
+        return step, [x], planner.launches_per_step
     # launches of this library's kernels per step (router tail 1 + route 3 + gather 1 + 2 GEMMs
     # + combine 1); the router GEMM runs in cuBLAS through torch
     if kind == "gpt_oss":
@@ -530,6 +532,22 @@ def run_ours(args):
         hot = {"ms_per_step": round(hot_ms / args.steps, 4),
                "value": round(cfg.tokens * args.steps / (hot_ms / 1e3), 1), "unit": "tokens/s"}
 
+    phases = None
+    if world > 1 and hasattr(step, "planner"):
+        # per-phase device times of the EP step (CUDA events between the phases' launches, L2
+        # flushed before each step), median over steps, max over ranks
+        planner = step.planner
+        rows = []
+        for _ in range(max(3, min(args.steps, 10))):
+            flush.zero_()
+            planner.timing = []
+            step(*inputs)
+            rows.append(planner.phase_ms())
+        planner.timing = None
+        names = list(rows[0].keys())
+        med = torch.tensor([statistics.median(r[n] for r in rows) for n in names], device=device)
+        dist.all_reduce(med, op=dist.ReduceOp.MAX)
+        phases = {n: round(float(v), 4) for n, v in zip(names, med.tolist())}
     tokens = cfg.tokens
     ms_per_step = total_ms / args.steps
     value = tokens * args.steps / (total_ms / 1e3)
@@ -567,6 +585,7 @@ def run_ours(args):
             "clocks": clocks.summary(),
             "op_roofline_ms": round(op_roofline_ms(cfg, case), 4),
             "configs": configs,
+            "ep_phases_ms": phases,
         }
         print(json.dumps(line), flush=True)
     if world > 1:

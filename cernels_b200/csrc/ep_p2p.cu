@@ -3,23 +3,29 @@
 // The reference is single-GPU; expert parallelism is this build's multi-GPU scheme. Each
 // rank owns one device window (cudaMalloc), mapped into every other rank's address space
 // with CUDA IPC:
-//   hdr[R]          one EpHeader per peer rank
-//   recv[R][cap][H] rows routed to this rank's experts, one slot per source rank
+//   hdr[R]          one EpHeader per peer rank (its counts and flags for this rank)
+//   recv[R*cap][H]  rows routed to this rank's experts, expert-contiguous: all sources' rows of
+//                   local expert 0 (source 0 first), then expert 1, ...
 //   back[cap][H]    expert outputs of this rank's own routed rows, written by their owners
 // One step (epoch e, all kernels on the caller's stream):
-//   ep_dispatch  source: per destination d, writes the per-expert row counts into
-//                d.hdr[me], copies its routed rows (gathered from x) into d.recv[me][i],
-//                then — after every CTA fenced — release-stores d.hdr[me].data_epoch = e
-//   ep_segments  destination: waits (acquire, bounded) for data_epoch == e from every source,
-//                builds the grouped-GEMM tables: group (s, local expert) -> rows in recv[s]
+//   ep_counts    source, one CTA per destination d: writes its per-expert row counts into
+//                d.hdr[me], release-stores count_epoch = e, waits (acquire, bounded) until
+//                every source's counts for e are in d's window, and computes where its rows
+//                of each expert start in d's receive region
+//   ep_dispatch  source: copies its routed rows (gathered from x) to those positions, work
+//                interleaved over destinations; then — after every CTA fenced — release-stores
+//                d.hdr[me].data_epoch = e
+//   ep_segments  destination: waits for data_epoch == e from every source, builds the
+//                grouped-GEMM tables (one group per local expert, no partial tiles between
+//                sources) and the per-source prefix tables of the return
 //   2 x grouped_gemm_kernel on recv (tcgen05/TMA, in place)
 //   ep_return    destination: writes each result row into its source's back[seg_start + i],
-//                then release-stores s.hdr[me].result_epoch = e
+//                interleaved over sources, then release-stores s.hdr[me].result_epoch = e
 //   ep_combine   source: waits (acquire, bounded) for result_epoch == e from every destination,
 //                out[t] = bf16(sum_j w[t, j] * back[inv[t, j]]) in slot order
 // A rank starts step e+1 only after its combine of step e saw every destination's results,
 // and a destination signals results only after its GEMMs finished reading recv, so no slot
-// is overwritten while in use. Loads and stores are plain 16-byte accesses (no TMA and no
+// or header is overwritten while in use. Loads and stores are plain accesses (no TMA and no
 // multicast on peer memory). Every wait gives up after a limit (5 s unless
 // cernels_set_wait_limit_ns set another) and records a status.
 #include <cstdio>
@@ -40,6 +46,7 @@ struct __align__(256) EpHeader {
   int32_t counts[kEpMaxLocalExperts];  // rows per local expert sent by this peer
   int32_t seg_start;                   // first routed row of this segment at the source
   int32_t n_rows;                      // rows in the segment
+  uint32_t count_epoch;                // counts above are those of this step (written by the source)
   uint32_t data_epoch;                 // written by the source (destination's window)
   uint32_t result_epoch;               // written by the destination (source's window)
 };
@@ -90,132 +97,221 @@ __device__ bool last_cta_done(unsigned* counter) {
   return last != 0;
 }
 
+// Block-wide exclusive scan of one int per thread (blockDim.x <= 1024); returns the thread's
+// exclusive prefix and writes the block total to *total.
+__device__ int block_exclusive_scan(int v, int* warp_tot, int* total) {
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  int incl = v;
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int n = __shfl_up_sync(0xffffffffu, incl, o);
+    if (lane >= o) incl += n;
+  }
+  if (lane == 31) warp_tot[warp] = incl;
+  __syncthreads();
+  if (warp == 0) {
+    const int nw = (blockDim.x + 31) >> 5;
+    const int wv = lane < nw ? warp_tot[lane] : 0;
+    int wi = wv;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int n = __shfl_up_sync(0xffffffffu, wi, o);
+      if (lane >= o) wi += n;
+    }
+    warp_tot[lane] = wi - wv;
+    if (lane == 31) warp_tot[32] = wi;
+  }
+  __syncthreads();
+  const int excl = warp_tot[warp] + incl - v;
+  *total = warp_tot[32];
+  __syncthreads();
+  return excl;
+}
+
+// Step 1 of a dispatch, one CTA per destination d: publish this rank's per-expert row counts in
+// d's window, wait (bounded) until every source has published its counts for this step, and
+// compute where this rank's rows go in d's expert-contiguous receive region:
+//   dest_off[d][e] = rows of d's experts < e from all sources + rows of expert e from sources < me.
+__global__ void __launch_bounds__(kEpThreads) ep_counts_kernel(uint8_t* const* __restrict__ peers, EpGeometry g,
+                                                               const int* __restrict__ offsets, uint32_t epoch,
+                                                               int* __restrict__ dest_off, int* status) {
+  __shared__ int cnt[kEpMaxLocalExperts];  // per expert: rows from all sources
+  __shared__ int before[kEpMaxLocalExperts];  // per expert: rows from sources < me
+  __shared__ int warp_tot[33];
+  __shared__ int ok;
+  const int d = blockIdx.x, El = g.local_experts;
+  EpHeader* h = hdr_of(peers[d], g.rank);
+  for (int e = threadIdx.x; e < El; e += blockDim.x) h->counts[e] = offsets[d * El + e + 1] - offsets[d * El + e];
+  if (threadIdx.x == 0) {
+    h->seg_start = offsets[d * El];
+    h->n_rows = offsets[(d + 1) * El] - offsets[d * El];
+    ok = 1;
+  }
+  __threadfence_system();
+  __syncthreads();
+  if (threadIdx.x == 0) st_release_sys(&h->count_epoch, epoch);
+  if (threadIdx.x < g.world)
+    if (!wait_epoch(&hdr_of(peers[d], threadIdx.x)->count_epoch, epoch, status, kStatusTimeoutOther, g.wait_ns))
+      ok = 0;
+  __syncthreads();
+  for (int e = threadIdx.x; e < El; e += blockDim.x) {
+    int tot = 0, bef = 0;
+    if (ok)
+      for (int s = 0; s < g.world; ++s) {
+        const int c = __ldcv(&hdr_of(peers[d], s)->counts[e]);
+        tot += c;
+        if (s < g.rank) bef += c;
+      }
+    cnt[e] = tot;
+    before[e] = bef;
+  }
+  __syncthreads();
+  int carry = 0;
+  for (int e0 = 0; e0 < El; e0 += blockDim.x) {
+    const int e = e0 + threadIdx.x;
+    int total = 0;
+    const int excl = block_exclusive_scan(e < El ? cnt[e] : 0, warp_tot, &total);
+    if (e < El) dest_off[d * kEpMaxLocalExperts + e] = carry + excl + before[e];
+    carry += total;
+  }
+}
+
+// Step 2: copy every routed row x[perm_token[p]] to its slot in its owner's receive region.
+// Work items are interleaved over destinations, starting at rank + 1, so the sources do not
+// all write to the same destination at the same time.
 __global__ void __launch_bounds__(kEpThreads) ep_dispatch_kernel(uint8_t* const* __restrict__ peers, EpGeometry g,
                                                                  const uint4* __restrict__ x,
                                                                  const int* __restrict__ perm_token,
-                                                                 const int* __restrict__ offsets, uint32_t epoch,
+                                                                 const int* __restrict__ offsets,
+                                                                 const int* __restrict__ dest_off, uint32_t epoch,
                                                                  unsigned* __restrict__ counter, int* status) {
-  const int El = g.local_experts;
-  if (blockIdx.x == 0) {
-    for (int i = threadIdx.x; i < g.world * El; i += blockDim.x) {
-      const int d = i / El, e = i - d * El;
-      hdr_of(peers[d], g.rank)->counts[e] = offsets[d * El + e + 1] - offsets[d * El + e];
-    }
-    for (int d = threadIdx.x; d < g.world; d += blockDim.x) {
-      EpHeader* h = hdr_of(peers[d], g.rank);
-      h->seg_start = offsets[d * El];
-      h->n_rows = offsets[(d + 1) * El] - offsets[d * El];
-    }
-  }
-  const int total = offsets[g.world * El];
+  const int El = g.local_experts, R = g.world;
+  int max_n = 0;
+  for (int d = 0; d < R; ++d) max_n = max(max_n, offsets[(d + 1) * El] - offsets[d * El]);
   const int vec = g.hidden / 8;
+  const long long cap_rows = static_cast<long long>(R) * g.cap;
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
   const int n_warps = (gridDim.x * blockDim.x) >> 5;
-  for (int p = warp; p < total; p += n_warps) {
-    int d = 0;
-    while (d + 1 < g.world && offsets[(d + 1) * El] <= p) ++d;
-    const int i = p - offsets[d * El];
-    if (i >= g.cap) {  // cannot happen when cap >= tokens * topk; skip rather than overrun
+  const long long items = static_cast<long long>(max_n) * R;
+  for (long long q = warp; q < items; q += n_warps) {
+    const int i = static_cast<int>(q / R);
+    const int d = (g.rank + 1 + static_cast<int>(q % R)) % R;
+    const int lo = offsets[d * El];
+    if (i >= offsets[(d + 1) * El] - lo) continue;
+    const int p = lo + i;
+    // local expert of row p: last e with offsets[d*El + e] <= p
+    int a = 0, b = El - 1;
+    while (a < b) {
+      const int m = (a + b + 1) >> 1;
+      if (offsets[d * El + m] <= p) a = m; else b = m - 1;
+    }
+    const long long dst_row = static_cast<long long>(dest_off[d * kEpMaxLocalExperts + a]) + (p - offsets[d * El + a]);
+    if (dst_row < 0 || dst_row >= cap_rows) {  // cannot happen with consistent counts; never overrun
       if (lane == 0) atomicCAS(status, 0, kStatusTimeoutOther);
       continue;
     }
     const uint4* src = x + static_cast<size_t>(perm_token[p]) * vec;
-    uint4* dst = reinterpret_cast<uint4*>(peers[d] + g.recv_offset) +
-                 (static_cast<size_t>(g.rank) * g.cap + i) * vec;
+    uint4* dst = reinterpret_cast<uint4*>(peers[d] + g.recv_offset) + static_cast<size_t>(dst_row) * vec;
     for (int v = lane; v < vec; v += 32) dst[v] = src[v];
   }
-  if (last_cta_done(counter) && threadIdx.x < g.world)
+  if (last_cta_done(counter) && threadIdx.x < R)
     st_release_sys(&hdr_of(peers[threadIdx.x], g.rank)->data_epoch, epoch);
 }
 
-// One CTA of 1024 threads: wait for every source, then group tables.
+// One CTA of 1024 threads at the destination: wait for every source, then the grouped-GEMM
+// tables (group = local expert, rows of all sources contiguous) and, per source, the prefix of
+// its segment by expert (for the return).
+//   offsets[e], mtile_offsets[e]  (El + 1 entries)
+//   src_prefix[s][e]              rows of source s's segment before expert e (El + 1 entries)
+//   run_start[e][s]               first receive row of source s's rows of expert e
 __global__ void __launch_bounds__(1024) ep_segments_kernel(uint8_t* __restrict__ window, EpGeometry g, uint32_t epoch,
-                                                           int* __restrict__ offsets, int* __restrict__ group_rows,
-                                                           int* __restrict__ mtile_offsets, int* status) {
+                                                           int* __restrict__ offsets, int* __restrict__ mtile_offsets,
+                                                           int* __restrict__ src_prefix, int* __restrict__ run_start,
+                                                           int* status) {
   __shared__ int ok;
-  __shared__ int warp_tot[32];
-  __shared__ int carry;
-  if (threadIdx.x == 0) {
-    ok = 1;
-    carry = 0;
-  }
+  __shared__ int warp_tot[33];
+  const int El = g.local_experts, R = g.world;
+  if (threadIdx.x == 0) ok = 1;
   __syncthreads();
-  if (threadIdx.x < g.world)
+  if (threadIdx.x < R)
     if (!wait_epoch(&hdr_of(window, threadIdx.x)->data_epoch, epoch, status, kStatusTimeoutOther, g.wait_ns)) ok = 0;
   __syncthreads();
   fence_proxy_async_global();  // peer-written rows are read next by TMA (async proxy)
-  const int El = g.local_experts, G = g.world * El;
-  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-  for (int g0 = 0; g0 < G; g0 += 1024) {
-    const int gi = g0 + threadIdx.x;
-    int rows = 0, start = 0;
-    if (gi < G && ok) {
-      const int s = gi / El, e = gi - s * El;
-      const EpHeader* h = hdr_of(window, s);
-      for (int j = 0; j < e; ++j) start += h->counts[j];
-      rows = h->counts[e];
-      // clamp to this source's slot of the window
-      start = min(max(start, 0), g.cap);
-      rows = min(max(rows, 0), g.cap - start);
-      start += s * g.cap;
-    }
+  const long long cap_rows = static_cast<long long>(R) * g.cap;
+  int carry_rows = 0, carry_tiles = 0;
+  for (int e0 = 0; e0 < El; e0 += blockDim.x) {
+    const int e = e0 + threadIdx.x;
+    int rows = 0;
+    if (e < El && ok)
+      for (int s = 0; s < R; ++s) rows += max(hdr_of(window, s)->counts[e], 0);
+    int total_rows = 0, total_tiles = 0;
+    const int row_excl = block_exclusive_scan(rows, warp_tot, &total_rows);
     const int tiles = (rows + kBlockM - 1) / kBlockM;
-    // block exclusive scan of tiles
-    int incl = tiles;
-#pragma unroll
-    for (int o = 1; o < 32; o <<= 1) {
-      const int n = __shfl_up_sync(0xffffffffu, incl, o);
-      if (lane >= o) incl += n;
-    }
-    if (lane == 31) warp_tot[warp] = incl;
-    __syncthreads();
-    if (warp == 0) {
-      const int wv = warp_tot[lane];
-      int wi = wv;
-#pragma unroll
-      for (int o = 1; o < 32; o <<= 1) {
-        const int n = __shfl_up_sync(0xffffffffu, wi, o);
-        if (lane >= o) wi += n;
+    const int tile_excl = block_exclusive_scan(tiles, warp_tot, &total_tiles);
+    if (e < El) {
+      // clamp so that a bad header can never make the GEMM read past the receive region
+      const long long start = min(static_cast<long long>(carry_rows + row_excl), cap_rows);
+      offsets[e] = static_cast<int>(start);
+      mtile_offsets[e] = carry_tiles + tile_excl;
+      int r = static_cast<int>(start);
+      for (int s = 0; s < R; ++s) {
+        run_start[e * R + s] = r;
+        r += ok ? max(hdr_of(window, s)->counts[e], 0) : 0;
       }
-      warp_tot[lane] = wi - wv;
     }
-    __syncthreads();
-    const int excl = carry + warp_tot[warp] + incl - tiles;
-    if (gi < G) {
-      offsets[gi] = start;
-      group_rows[gi] = rows;
-      mtile_offsets[gi] = excl;
+    carry_rows += total_rows;
+    carry_tiles += total_tiles;
+  }
+  for (int s = threadIdx.x; s < R; s += blockDim.x) {
+    int acc = 0;
+    for (int e = 0; e < El; ++e) {
+      src_prefix[s * (El + 1) + e] = acc;
+      acc += ok ? max(hdr_of(window, s)->counts[e], 0) : 0;
     }
-    __syncthreads();
-    if (threadIdx.x == 1023) carry = excl + tiles;
-    __syncthreads();
+    src_prefix[s * (El + 1) + El] = acc;
   }
   if (threadIdx.x == 0) {
-    mtile_offsets[G] = carry;
-    offsets[G] = g.world * g.cap;
+    offsets[El] = static_cast<int>(min(static_cast<long long>(carry_rows), cap_rows));
+    mtile_offsets[El] = carry_tiles;
   }
 }
 
+// Destination: every result row back to its source's return region, rows interleaved over
+// sources starting at rank + 1. Source s's segment is ordered by expert; its row i of expert e
+// sits at receive row run_start[e][s] + (i - src_prefix[s][e]).
 __global__ void __launch_bounds__(kEpThreads) ep_return_kernel(uint8_t* const* __restrict__ peers, EpGeometry g,
-                                                               const uint4* __restrict__ rows, uint32_t epoch,
+                                                               const uint4* __restrict__ rows,
+                                                               const int* __restrict__ src_prefix,
+                                                               const int* __restrict__ run_start, uint32_t epoch,
                                                                unsigned* __restrict__ counter) {
   uint8_t* own = peers[g.rank];
+  const int El = g.local_experts, R = g.world;
   const int vec = g.hidden / 8;
+  const long long cap_rows = static_cast<long long>(R) * g.cap;
+  int max_n = 0;
+  for (int s = 0; s < R; ++s) max_n = max(max_n, src_prefix[s * (El + 1) + El]);
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
   const int n_warps = (gridDim.x * blockDim.x) >> 5;
-  for (int s = 0; s < g.world; ++s) {
-    const EpHeader* h = hdr_of(own, s);
-    // Headers come from another rank: clamp to the window so a bad value cannot overrun it.
-    const int base = min(max(h->seg_start, 0), g.cap);
-    const int n = min(max(h->n_rows, 0), min(g.cap - base, g.cap));
-    uint4* dst = reinterpret_cast<uint4*>(peers[s] + g.back_offset);
-    for (int i = warp; i < n; i += n_warps) {
-      const uint4* src = rows + (static_cast<size_t>(s) * g.cap + i) * vec;
-      uint4* o = dst + static_cast<size_t>(base + i) * vec;
-      for (int v = lane; v < vec; v += 32) o[v] = src[v];
+  const long long items = static_cast<long long>(max_n) * R;
+  for (long long q = warp; q < items; q += n_warps) {
+    const int i = static_cast<int>(q / R);
+    const int s = (g.rank + 1 + static_cast<int>(q % R)) % R;
+    const int* pre = src_prefix + s * (El + 1);
+    if (i >= pre[El]) continue;
+    int a = 0, b = El - 1;
+    while (a < b) {
+      const int m = (a + b + 1) >> 1;
+      if (pre[m] <= i) a = m; else b = m - 1;
     }
+    const long long src_row = static_cast<long long>(run_start[a * R + s]) + (i - pre[a]);
+    // headers come from another rank: clamp to the windows so a bad value cannot overrun them
+    const int base = min(max(hdr_of(own, s)->seg_start, 0), g.cap);
+    if (src_row < 0 || src_row >= cap_rows || base + i >= g.cap) continue;
+    const uint4* src = rows + static_cast<size_t>(src_row) * vec;
+    uint4* o = reinterpret_cast<uint4*>(peers[s] + g.back_offset) + static_cast<size_t>(base + i) * vec;
+    for (int v = lane; v < vec; v += 32) o[v] = src[v];
   }
-  if (last_cta_done(counter) && threadIdx.x < g.world)
+  if (last_cta_done(counter) && threadIdx.x < R)
     st_release_sys(&hdr_of(peers[threadIdx.x], g.rank)->result_epoch, epoch);
 }
 
@@ -271,6 +367,7 @@ struct cernels_ep_ctx {
   uint8_t** d_peers;
   unsigned* d_counters;  // [0] dispatch, [1] return
   int* d_status;
+  int* d_dest_off;       // [kEpMaxRanks][kEpMaxLocalExperts] this rank's write offsets per destination
   bool connected;
 };
 
@@ -324,11 +421,13 @@ int cernels_ep_create(int32_t rank, int32_t world, int32_t hidden, int32_t local
   if (err == cudaSuccess) err = cudaMalloc(&c->d_peers, sizeof(uint8_t*) * kEpMaxRanks);
   if (err == cudaSuccess) err = cudaMalloc(&c->d_counters, 2 * sizeof(unsigned) + sizeof(int));
   if (err == cudaSuccess) err = cudaMemset(c->d_counters, 0, 2 * sizeof(unsigned) + sizeof(int));
+  if (err == cudaSuccess) err = cudaMalloc(&c->d_dest_off, sizeof(int) * kEpMaxRanks * kEpMaxLocalExperts);
   if (err == cudaSuccess) err = cudaIpcGetMemHandle(reinterpret_cast<cudaIpcMemHandle_t*>(handle_out), c->window);
   if (err != cudaSuccess) {
     if (c->window) cudaFree(c->window);
     if (c->d_peers) cudaFree(c->d_peers);
     if (c->d_counters) cudaFree(c->d_counters);
+    if (c->d_dest_off) cudaFree(c->d_dest_off);
     delete c;
     return rc_of(err);
   }
@@ -364,6 +463,7 @@ int cernels_ep_destroy(void* ctx) {
   cudaFree(c->window);
   cudaFree(c->d_peers);
   cudaFree(c->d_counters);
+  cudaFree(c->d_dest_off);
   delete c;
   return CERNELS_OK;
 }
@@ -375,21 +475,52 @@ int cernels_ep_dispatch(void* ctx, const void* x, const int32_t* perm_token, con
   if (rows > c->geo.cap) return CERNELS_E_UNSUPPORTED;
   if (rows > 0 && (!x || !perm_token || !offsets)) return CERNELS_E_NULL;
   if (x && (reinterpret_cast<uintptr_t>(x) & 15)) return CERNELS_E_ALIGNMENT;
-  ep_dispatch_kernel<<<ep_grid(rows), kEpThreads, 0, static_cast<cudaStream_t>(stream)>>>(
-      c->d_peers, geo_now(c), static_cast<const uint4*>(x), perm_token, offsets, epoch, c->d_counters, c->d_status);
+  cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const EpGeometry g = geo_now(c);
+  ep_counts_kernel<<<c->geo.world, kEpThreads, 0, st>>>(c->d_peers, g, offsets, epoch, c->d_dest_off, c->d_status);
+  ep_dispatch_kernel<<<ep_grid(rows), kEpThreads, 0, st>>>(c->d_peers, g, static_cast<const uint4*>(x), perm_token,
+                                                          offsets, c->d_dest_off, epoch, c->d_counters, c->d_status);
   return rc_of(cudaGetLastError());
 }
+
+namespace {
+// Tables of the receive side, carved out of the experts workspace.
+struct EpTables {
+  int *offsets, *mtile, *src_prefix, *run_start;
+  __nv_bfloat16 *glu, *down_out;
+};
+size_t ep_tables(const cernels_ep_ctx* c, int inter, uint8_t* base, EpTables* t) {
+  const size_t rows = static_cast<size_t>(c->geo.world) * c->geo.cap;
+  const size_t El = c->geo.local_experts, R = c->geo.world;
+  size_t off = 0;
+  auto take = [&](size_t bytes) {
+    off = align_up(off, 256);
+    uint8_t* p = base ? base + off : nullptr;
+    off += bytes;
+    return p;
+  };
+  uint8_t* p_off = take((El + 1) * 4);
+  uint8_t* p_mt = take((El + 1) * 4);
+  uint8_t* p_pre = take(R * (El + 1) * 4);
+  uint8_t* p_run = take(R * El * 4);
+  uint8_t* p_glu = take(rows * inter * 2);
+  uint8_t* p_down = take(rows * c->geo.hidden * 2);
+  if (t) {
+    t->offsets = reinterpret_cast<int*>(p_off);
+    t->mtile = reinterpret_cast<int*>(p_mt);
+    t->src_prefix = reinterpret_cast<int*>(p_pre);
+    t->run_start = reinterpret_cast<int*>(p_run);
+    t->glu = reinterpret_cast<__nv_bfloat16*>(p_glu);
+    t->down_out = reinterpret_cast<__nv_bfloat16*>(p_down);
+  }
+  return off + 256;
+}
+}  // namespace
 
 int cernels_ep_experts_workspace_bytes(void* ctx, const cernels_moe_shape* shape, size_t* bytes) {
   auto* c = static_cast<cernels_ep_ctx*>(ctx);
   if (!c || !shape || !bytes) return CERNELS_E_NULL;
-  const size_t rows = static_cast<size_t>(c->geo.world) * c->geo.cap;
-  const size_t G = static_cast<size_t>(c->geo.world) * c->geo.local_experts;
-  size_t off = 0;
-  off = align_up(off, 256) + (G + 1) * 4 * 3;  // offsets, group rows, tile offsets
-  off = align_up(off, 256) + rows * shape->intermediate * 2;
-  off = align_up(off, 256) + rows * c->geo.hidden * 2;
-  *bytes = off + 256;
+  *bytes = ep_tables(c, shape->intermediate, nullptr, nullptr);
   return CERNELS_OK;
 }
 
@@ -402,22 +533,16 @@ int cernels_ep_experts(void* ctx, const cernels_moe_shape* shape, const void* ga
   if (s.hidden != c->geo.hidden || s.experts != c->geo.local_experts || s.intermediate <= 0 ||
       s.intermediate % 8)
     return CERNELS_E_INVALID_SHAPE;
-  size_t need = 0;
-  cernels_ep_experts_workspace_bytes(ctx, shape, &need);
-  if (workspace_bytes < need) return CERNELS_E_WORKSPACE;
+  if (workspace_bytes < ep_tables(c, s.intermediate, nullptr, nullptr)) return CERNELS_E_WORKSPACE;
   cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
-  const int G = c->geo.world * c->geo.local_experts;
+  EpTables t;
+  ep_tables(c, s.intermediate, static_cast<uint8_t*>(workspace), &t);
+  const EpGeometry g = geo_now(c);
+  const int El = c->geo.local_experts;
   const size_t rows = static_cast<size_t>(c->geo.world) * c->geo.cap;
-  uint8_t* base = static_cast<uint8_t*>(workspace);
-  int* offsets = reinterpret_cast<int*>(base);
-  int* group_rows = offsets + (G + 1);
-  int* mtile = group_rows + (G + 1);
-  size_t off = align_up((G + 1) * 4 * 3, 256);
-  __nv_bfloat16* glu = reinterpret_cast<__nv_bfloat16*>(base + off);
-  off = align_up(off + rows * s.intermediate * 2, 256);
-  __nv_bfloat16* down_out = reinterpret_cast<__nv_bfloat16*>(base + off);
 
-  ep_segments_kernel<<<1, 1024, 0, stream>>>(c->window, geo_now(c), epoch, offsets, group_rows, mtile, c->d_status);
+  ep_segments_kernel<<<1, 1024, 0, stream>>>(c->window, g, epoch, t.offsets, t.mtile, t.src_prefix, t.run_start,
+                                             c->d_status);
   cudaError_t err = cudaGetLastError();
   if (err != cudaSuccess) return rc_of(err);
   const bool gptoss = s.layout == CERNELS_LAYOUT_GPTOSS;
@@ -426,31 +551,31 @@ int cernels_ep_experts(void* ctx, const cernels_moe_shape* shape, const void* ga
   g1.a = reinterpret_cast<const __nv_bfloat16*>(c->window + c->geo.recv_offset);
   g1.b = static_cast<const __nv_bfloat16*>(gate_up_proj);
   g1.bias = gptoss ? gate_up_bias : nullptr;
-  g1.out = glu;
-  g1.offsets = offsets;
-  g1.mtile_offsets = mtile;
-  g1.group_rows = group_rows;
+  g1.out = t.glu;
+  g1.offsets = t.offsets;
+  g1.mtile_offsets = t.mtile;
   g1.status = c->d_status;
   g1.rows = static_cast<int>(rows);
-  g1.experts = G;
+  g1.experts = El;
   g1.k = s.hidden;
   g1.n = 2 * s.intermediate;
   g1.out_cols = s.intermediate;
-  g1.weight_experts = s.experts;
+  g1.weight_experts = El;
   if ((err = launch_grouped_gemm(gptoss ? kGateUpGptOss : kGateUpLinear, g1, sms, stream)) != cudaSuccess)
     return rc_of(err);
   GroupedGemmArgs g2 = g1;
-  g2.a = glu;
+  g2.a = t.glu;
   g2.b = static_cast<const __nv_bfloat16*>(down_proj);
   g2.bias = gptoss ? down_bias : nullptr;
-  g2.out = down_out;
+  g2.out = t.down_out;
   g2.k = s.intermediate;
   g2.n = s.hidden;
   g2.out_cols = s.hidden;
   if ((err = launch_grouped_gemm(gptoss ? kDownGptOss : kDownLinear, g2, sms, stream)) != cudaSuccess)
     return rc_of(err);
   ep_return_kernel<<<ep_grid(static_cast<int>(c->geo.cap)), kEpThreads, 0, stream>>>(
-      c->d_peers, geo_now(c), reinterpret_cast<const uint4*>(down_out), epoch, c->d_counters + 1);
+      c->d_peers, g, reinterpret_cast<const uint4*>(t.down_out), t.src_prefix, t.run_start, epoch,
+      c->d_counters + 1);
   return rc_of(cudaGetLastError());
 }
 

@@ -106,7 +106,7 @@ class P2PTransport:
         self._lib.check(self._lib.load().cernels_ep_status(self.ctx, ctypes.byref(st)), "cernels_ep_status")
         return int(st.value)
 
-    def step(self, x, perm_token, offsets, inv, w, weights, shape):
+    def step(self, x, perm_token, offsets, inv, w, weights, shape, mark=lambda: None):
         """dispatch -> grouped experts -> return -> combine for one batch; returns [T, H] bf16."""
         import ctypes
 
@@ -120,6 +120,7 @@ class P2PTransport:
         ptr = lambda t: None if t is None else t.data_ptr()  # noqa: E731
         self._lib.check(lib.cernels_ep_dispatch(self.ctx, x.data_ptr(), perm_token.data_ptr(), offsets.data_ptr(),
                                                 T * k, self.epoch, stream), "cernels_ep_dispatch")
+        mark()
         n = ctypes.c_size_t(0)
         self._lib.check(lib.cernels_ep_experts_workspace_bytes(self.ctx, ctypes.byref(shape), ctypes.byref(n)),
                         "cernels_ep_experts_workspace_bytes")
@@ -128,9 +129,11 @@ class P2PTransport:
         self._lib.check(lib.cernels_ep_experts(self.ctx, ctypes.byref(shape), w1.data_ptr(), ptr(b1), w2.data_ptr(),
                                                ptr(b2), self.epoch, self._ws.data_ptr(), n.value, stream),
                         "cernels_ep_experts")
+        mark()
         out = torch.empty(T, x.shape[1], dtype=x.dtype, device=x.device)
         self._lib.check(lib.cernels_ep_combine(self.ctx, inv.data_ptr(), w.data_ptr(), T, k, out.data_ptr(),
                                                self.epoch, stream), "cernels_ep_combine")
+        mark()
         return out
 
     def __del__(self):
@@ -232,14 +235,36 @@ class ExpertParallelMoe:
             return self.forward_p2p(x)
         return self.forward_nccl(x)
 
+    PHASES = ("router", "route", "dispatch", "experts", "combine", "shared")
+
+    def _mark(self):
+        """Records a CUDA event on the current stream when phase timing is on (self.timing)."""
+        if getattr(self, "timing", None) is not None:
+            ev = torch.cuda.Event(enable_timing=True)
+            ev.record()
+            self.timing.append(ev)
+
+    def phase_ms(self):
+        """Per-phase device times (ms) of the last timed forward (PHASES order; the shared
+        expert's phase is 0 when there is none). Synchronises."""
+        ev = self.timing
+        torch.cuda.synchronize()
+        out = [a.elapsed_time(b) for a, b in zip(ev[:-1], ev[1:])]
+        return dict(zip(self.PHASES, out + [0.0] * (len(self.PHASES) - len(out))))
+
     def forward_p2p(self, x: torch.Tensor) -> torch.Tensor:
         from . import _lib
 
+        if getattr(self, "timing", None) is not None:
+            self.timing = []
         with torch.no_grad():
+            self._mark()
             idx, w = self.router(x)
             idx = idx.to(torch.int32).contiguous()
             w = w.float().contiguous()
+            self._mark()
             offsets, perm_token, _perm_weight, inv = self.backend.route(idx, w, self.E)
+            self._mark()
             if self._p2p is None:
                 # window capacity: the most routed rows any rank can send (all ranks agree)
                 cap = torch.tensor([idx.numel()], dtype=torch.int64, device=x.device)
@@ -250,9 +275,11 @@ class ExpertParallelMoe:
             F = w1.shape[1] // 2 if layout == 0 else w1.shape[2] // 2
             shape = _lib.MoeShape(int(self._p2p.max_rows), int(x.shape[1]), int(self.E // self.world), int(F), 1,
                                   int(layout))
-            out = self._p2p.step(x.contiguous(), perm_token, offsets, inv, w, self.local_weights, shape)
+            out = self._p2p.step(x.contiguous(), perm_token, offsets, inv, w, self.local_weights, shape,
+                                 mark=self._mark)
             if self.shared is not None:
                 out = out + self.shared(x)
+                self._mark()
             return out
 
     def forward_nccl(self, x: torch.Tensor) -> torch.Tensor:
