@@ -506,8 +506,9 @@ def run_ours(args):
         dist.barrier()
     torch.cuda.synchronize()
     log("timed region")
+    use_graph = args.graph
     with ClockSampler(local) as clocks:
-        total_ms, per = time_device(step, inputs, args.steps, warmup, flush, graph=args.graph)
+        total_ms, per = time_device(step, inputs, args.steps, warmup, flush, graph=use_graph)
     log(f"clock samples: {len(clocks.samples)} ({clocks.error})")
     torch.cuda.synchronize()
     if world > 1:
@@ -576,7 +577,7 @@ def run_ours(args):
             "config": {"workload": cfg.name, "tokens": cfg.tokens, "hidden": cfg.hidden, "experts": cfg.experts,
                        "intermediate": cfg.inter, "topk": cfg.topk, "shared_intermediate": cfg.shared_inter,
                        "parallelism": f"ep{world}" if (world > 1 and cfg.name in EP_CONFIGS) else f"replica{world}",
-                       "l2": "flushed (256 MB write) before every timed step", "graph": bool(args.graph)},
+                       "l2": "flushed (256 MB write) before every timed step", "graph": bool(use_graph)},
             "roofline": roof, "cpu_baseline": cpu,
             "e2e": {"value": round(e2e_value, 1), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h, "token_chunks": e2e_chunks},

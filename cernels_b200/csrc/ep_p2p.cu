@@ -73,6 +73,31 @@ __device__ bool wait_epoch(const uint32_t* flag, uint32_t epoch, int* status, in
   return true;
 }
 
+// The epoch of the current step: an explicit nonzero argument, or (argument 0) one past the
+// last step this rank completed, kept in device memory so that a step can be replayed from a
+// CUDA graph.
+__device__ __forceinline__ uint32_t step_epoch(const uint32_t* epoch_dev, uint32_t arg) {
+  return arg ? arg : *reinterpret_cast<const volatile uint32_t*>(epoch_dev) + 1u;
+}
+
+// Copies one row of `vec` 16-byte pieces with the whole warp: up to 8 loads per lane in flight
+// before their stores.
+__device__ __forceinline__ void copy_row(uint4* __restrict__ dst, const uint4* __restrict__ src, int vec, int lane) {
+  for (int v0 = 0; v0 < vec; v0 += 32 * 8) {
+    uint4 r[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int v = v0 + j * 32 + lane;
+      if (v < vec) r[j] = __ldcs(src + v);
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int v = v0 + j * 32 + lane;
+      if (v < vec) dst[v] = r[j];
+    }
+  }
+}
+
 __device__ __forceinline__ EpHeader* hdr_of(uint8_t* window, int peer) {
   return reinterpret_cast<EpHeader*>(window) + peer;
 }
@@ -133,8 +158,10 @@ __device__ int block_exclusive_scan(int v, int* warp_tot, int* total) {
 // compute where this rank's rows go in d's expert-contiguous receive region:
 //   dest_off[d][e] = rows of d's experts < e from all sources + rows of expert e from sources < me.
 __global__ void __launch_bounds__(kEpThreads) ep_counts_kernel(uint8_t* const* __restrict__ peers, EpGeometry g,
-                                                               const int* __restrict__ offsets, uint32_t epoch,
-                                                               int* __restrict__ dest_off, int* status) {
+                                                               const int* __restrict__ offsets, uint32_t epoch_arg,
+                                                               const uint32_t* epoch_dev, int* __restrict__ dest_off,
+                                                               int* status) {
+  const uint32_t epoch = step_epoch(epoch_dev, epoch_arg);
   __shared__ int cnt[kEpMaxLocalExperts];  // per expert: rows from all sources
   __shared__ int before[kEpMaxLocalExperts];  // per expert: rows from sources < me
   __shared__ int warp_tot[33];
@@ -183,8 +210,10 @@ __global__ void __launch_bounds__(kEpThreads) ep_dispatch_kernel(uint8_t* const*
                                                                  const uint4* __restrict__ x,
                                                                  const int* __restrict__ perm_token,
                                                                  const int* __restrict__ offsets,
-                                                                 const int* __restrict__ dest_off, uint32_t epoch,
-                                                                 unsigned* __restrict__ counter, int* status) {
+                                                                 const int* __restrict__ dest_off, uint32_t epoch_arg,
+                                                                 const uint32_t* epoch_dev, unsigned* __restrict__ counter,
+                                                                 int* status) {
+  const uint32_t epoch = step_epoch(epoch_dev, epoch_arg);
   const int El = g.local_experts, R = g.world;
   int max_n = 0;
   for (int d = 0; d < R; ++d) max_n = max(max_n, offsets[(d + 1) * El] - offsets[d * El]);
@@ -210,9 +239,8 @@ __global__ void __launch_bounds__(kEpThreads) ep_dispatch_kernel(uint8_t* const*
       if (lane == 0) atomicCAS(status, 0, kStatusTimeoutOther);
       continue;
     }
-    const uint4* src = x + static_cast<size_t>(perm_token[p]) * vec;
-    uint4* dst = reinterpret_cast<uint4*>(peers[d] + g.recv_offset) + static_cast<size_t>(dst_row) * vec;
-    for (int v = lane; v < vec; v += 32) dst[v] = src[v];
+    copy_row(reinterpret_cast<uint4*>(peers[d] + g.recv_offset) + static_cast<size_t>(dst_row) * vec,
+             x + static_cast<size_t>(perm_token[p]) * vec, vec, lane);
   }
   if (last_cta_done(counter) && threadIdx.x < R)
     st_release_sys(&hdr_of(peers[threadIdx.x], g.rank)->data_epoch, epoch);
@@ -224,10 +252,12 @@ __global__ void __launch_bounds__(kEpThreads) ep_dispatch_kernel(uint8_t* const*
 //   offsets[e], mtile_offsets[e]  (El + 1 entries)
 //   src_prefix[s][e]              rows of source s's segment before expert e (El + 1 entries)
 //   run_start[e][s]               first receive row of source s's rows of expert e
-__global__ void __launch_bounds__(1024) ep_segments_kernel(uint8_t* __restrict__ window, EpGeometry g, uint32_t epoch,
+__global__ void __launch_bounds__(1024) ep_segments_kernel(uint8_t* __restrict__ window, EpGeometry g,
+                                                           uint32_t epoch_arg, const uint32_t* epoch_dev,
                                                            int* __restrict__ offsets, int* __restrict__ mtile_offsets,
                                                            int* __restrict__ src_prefix, int* __restrict__ run_start,
                                                            int* status) {
+  const uint32_t epoch = step_epoch(epoch_dev, epoch_arg);
   __shared__ int ok;
   __shared__ int warp_tot[33];
   const int El = g.local_experts, R = g.world;
@@ -282,8 +312,9 @@ __global__ void __launch_bounds__(1024) ep_segments_kernel(uint8_t* __restrict__
 __global__ void __launch_bounds__(kEpThreads) ep_return_kernel(uint8_t* const* __restrict__ peers, EpGeometry g,
                                                                const uint4* __restrict__ rows,
                                                                const int* __restrict__ src_prefix,
-                                                               const int* __restrict__ run_start, uint32_t epoch,
-                                                               unsigned* __restrict__ counter) {
+                                                               const int* __restrict__ run_start, uint32_t epoch_arg,
+                                                               const uint32_t* epoch_dev, unsigned* __restrict__ counter) {
+  const uint32_t epoch = step_epoch(epoch_dev, epoch_arg);
   uint8_t* own = peers[g.rank];
   const int El = g.local_experts, R = g.world;
   const int vec = g.hidden / 8;
@@ -307,18 +338,22 @@ __global__ void __launch_bounds__(kEpThreads) ep_return_kernel(uint8_t* const* _
     // headers come from another rank: clamp to the windows so a bad value cannot overrun them
     const int base = min(max(hdr_of(own, s)->seg_start, 0), g.cap);
     if (src_row < 0 || src_row >= cap_rows || base + i >= g.cap) continue;
-    const uint4* src = rows + static_cast<size_t>(src_row) * vec;
-    uint4* o = reinterpret_cast<uint4*>(peers[s] + g.back_offset) + static_cast<size_t>(base + i) * vec;
-    for (int v = lane; v < vec; v += 32) o[v] = src[v];
+    copy_row(reinterpret_cast<uint4*>(peers[s] + g.back_offset) + static_cast<size_t>(base + i) * vec,
+             rows + static_cast<size_t>(src_row) * vec, vec, lane);
   }
   if (last_cta_done(counter) && threadIdx.x < R)
     st_release_sys(&hdr_of(peers[threadIdx.x], g.rank)->result_epoch, epoch);
 }
 
+// Last kernel of a step: with the device-side epoch (argument 0), its last CTA records the step
+// as completed.
 __global__ void __launch_bounds__(kEpThreads) ep_combine_kernel(uint8_t* __restrict__ window, EpGeometry g,
-                                                                uint32_t epoch, const int* __restrict__ inv,
+                                                                uint32_t epoch_arg, uint32_t* epoch_dev,
+                                                                unsigned* __restrict__ counter,
+                                                                const int* __restrict__ inv,
                                                                 const float* __restrict__ weights, int tokens,
                                                                 int topk, uint4* __restrict__ out, int* status) {
+  const uint32_t epoch = step_epoch(epoch_dev, epoch_arg);
   __shared__ int ok;
   if (threadIdx.x == 0) ok = 1;
   __syncthreads();
@@ -351,6 +386,7 @@ __global__ void __launch_bounds__(kEpThreads) ep_combine_kernel(uint8_t* __restr
       out[static_cast<size_t>(t) * vec + v] = o;
     }
   }
+  if (epoch_arg == 0 && last_cta_done(counter) && threadIdx.x == 0) *epoch_dev = epoch;
 }
 
 }  // namespace
@@ -365,7 +401,7 @@ struct cernels_ep_ctx {
   uint8_t* window;
   uint8_t* peers[kEpMaxRanks];
   uint8_t** d_peers;
-  unsigned* d_counters;  // [0] dispatch, [1] return
+  unsigned* d_counters;  // [0] dispatch, [1] return, [2] combine, [3] last completed epoch
   int* d_status;
   int* d_dest_off;       // [kEpMaxRanks][kEpMaxLocalExperts] this rank's write offsets per destination
   bool connected;
@@ -419,8 +455,8 @@ int cernels_ep_create(int32_t rank, int32_t world, int32_t hidden, int32_t local
   cudaError_t err = cudaMalloc(&c->window, c->window_bytes);
   if (err == cudaSuccess) err = cudaMemset(c->window, 0, c->geo.recv_offset);
   if (err == cudaSuccess) err = cudaMalloc(&c->d_peers, sizeof(uint8_t*) * kEpMaxRanks);
-  if (err == cudaSuccess) err = cudaMalloc(&c->d_counters, 2 * sizeof(unsigned) + sizeof(int));
-  if (err == cudaSuccess) err = cudaMemset(c->d_counters, 0, 2 * sizeof(unsigned) + sizeof(int));
+  if (err == cudaSuccess) err = cudaMalloc(&c->d_counters, 4 * sizeof(unsigned) + sizeof(int));
+  if (err == cudaSuccess) err = cudaMemset(c->d_counters, 0, 4 * sizeof(unsigned) + sizeof(int));
   if (err == cudaSuccess) err = cudaMalloc(&c->d_dest_off, sizeof(int) * kEpMaxRanks * kEpMaxLocalExperts);
   if (err == cudaSuccess) err = cudaIpcGetMemHandle(reinterpret_cast<cudaIpcMemHandle_t*>(handle_out), c->window);
   if (err != cudaSuccess) {
@@ -431,7 +467,7 @@ int cernels_ep_create(int32_t rank, int32_t world, int32_t hidden, int32_t local
     delete c;
     return rc_of(err);
   }
-  c->d_status = reinterpret_cast<int*>(c->d_counters + 2);
+  c->d_status = reinterpret_cast<int*>(c->d_counters + 4);
   c->peers[rank] = c->window;
   *ctx_out = c;
   return CERNELS_OK;
@@ -477,9 +513,11 @@ int cernels_ep_dispatch(void* ctx, const void* x, const int32_t* perm_token, con
   if (x && (reinterpret_cast<uintptr_t>(x) & 15)) return CERNELS_E_ALIGNMENT;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const EpGeometry g = geo_now(c);
-  ep_counts_kernel<<<c->geo.world, kEpThreads, 0, st>>>(c->d_peers, g, offsets, epoch, c->d_dest_off, c->d_status);
+  ep_counts_kernel<<<c->geo.world, kEpThreads, 0, st>>>(c->d_peers, g, offsets, epoch, c->d_counters + 3,
+                                                        c->d_dest_off, c->d_status);
   ep_dispatch_kernel<<<ep_grid(rows), kEpThreads, 0, st>>>(c->d_peers, g, static_cast<const uint4*>(x), perm_token,
-                                                          offsets, c->d_dest_off, epoch, c->d_counters, c->d_status);
+                                                          offsets, c->d_dest_off, epoch, c->d_counters + 3,
+                                                          c->d_counters, c->d_status);
   return rc_of(cudaGetLastError());
 }
 
@@ -541,8 +579,8 @@ int cernels_ep_experts(void* ctx, const cernels_moe_shape* shape, const void* ga
   const int El = c->geo.local_experts;
   const size_t rows = static_cast<size_t>(c->geo.world) * c->geo.cap;
 
-  ep_segments_kernel<<<1, 1024, 0, stream>>>(c->window, g, epoch, t.offsets, t.mtile, t.src_prefix, t.run_start,
-                                             c->d_status);
+  ep_segments_kernel<<<1, 1024, 0, stream>>>(c->window, g, epoch, c->d_counters + 3, t.offsets, t.mtile,
+                                             t.src_prefix, t.run_start, c->d_status);
   cudaError_t err = cudaGetLastError();
   if (err != cudaSuccess) return rc_of(err);
   const bool gptoss = s.layout == CERNELS_LAYOUT_GPTOSS;
@@ -575,7 +613,7 @@ int cernels_ep_experts(void* ctx, const cernels_moe_shape* shape, const void* ga
     return rc_of(err);
   ep_return_kernel<<<ep_grid(static_cast<int>(c->geo.cap)), kEpThreads, 0, stream>>>(
       c->d_peers, g, reinterpret_cast<const uint4*>(t.down_out), t.src_prefix, t.run_start, epoch,
-      c->d_counters + 1);
+      c->d_counters + 3, c->d_counters + 1);
   return rc_of(cudaGetLastError());
 }
 
@@ -587,7 +625,8 @@ int cernels_ep_combine(void* ctx, const int32_t* inv, const float* weights, int3
   if (tokens > 0 && (!inv || !weights || !out)) return CERNELS_E_NULL;
   const int blocks = tokens > 0 ? ep_grid(tokens) : 1;
   ep_combine_kernel<<<blocks, kEpThreads, 0, static_cast<cudaStream_t>(stream)>>>(
-      c->window, geo_now(c), epoch, inv, weights, tokens, topk, static_cast<uint4*>(out), c->d_status);
+      c->window, geo_now(c), epoch, c->d_counters + 3, c->d_counters + 2, inv, weights, tokens, topk,
+      static_cast<uint4*>(out), c->d_status);
   return rc_of(cudaGetLastError());
 }
 

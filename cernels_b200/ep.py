@@ -96,8 +96,7 @@ class P2PTransport:
         dist.barrier(group=group)
         self.device = device
         self.max_rows = max_rows
-        self.epoch = 0
-        self._ws = None
+        self._ws = None  # epochs are counted on the device (epoch argument 0): steps replay from CUDA graphs
 
     def status(self) -> int:
         import ctypes
@@ -115,11 +114,10 @@ class P2PTransport:
         if T * k > self.max_rows:
             raise RuntimeError(f"expert-parallel window holds {self.max_rows} routed rows, batch has {T * k}")
         layout, w1, b1, w2, b2 = weights
-        self.epoch += 1
         stream = torch.cuda.current_stream(self.device).cuda_stream
         ptr = lambda t: None if t is None else t.data_ptr()  # noqa: E731
         self._lib.check(lib.cernels_ep_dispatch(self.ctx, x.data_ptr(), perm_token.data_ptr(), offsets.data_ptr(),
-                                                T * k, self.epoch, stream), "cernels_ep_dispatch")
+                                                T * k, 0, stream), "cernels_ep_dispatch")
         mark()
         n = ctypes.c_size_t(0)
         self._lib.check(lib.cernels_ep_experts_workspace_bytes(self.ctx, ctypes.byref(shape), ctypes.byref(n)),
@@ -127,12 +125,12 @@ class P2PTransport:
         if self._ws is None or self._ws.numel() < n.value:
             self._ws = torch.empty(n.value, dtype=torch.uint8, device=self.device)
         self._lib.check(lib.cernels_ep_experts(self.ctx, ctypes.byref(shape), w1.data_ptr(), ptr(b1), w2.data_ptr(),
-                                               ptr(b2), self.epoch, self._ws.data_ptr(), n.value, stream),
+                                               ptr(b2), 0, self._ws.data_ptr(), n.value, stream),
                         "cernels_ep_experts")
         mark()
         out = torch.empty(T, x.shape[1], dtype=x.dtype, device=x.device)
         self._lib.check(lib.cernels_ep_combine(self.ctx, inv.data_ptr(), w.data_ptr(), T, k, out.data_ptr(),
-                                               self.epoch, stream), "cernels_ep_combine")
+                                               0, stream), "cernels_ep_combine")
         mark()
         return out
 

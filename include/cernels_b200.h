@@ -202,17 +202,21 @@ int cernels_moe_experts_decode_noalloc(const cernels_moe_shape* shape, const voi
                                        const int32_t* indices, const float* weights, void* out, void* stream);
 
 /* ---- Expert parallelism over NVLink peer memory (no counterpart in the reference, which is
- * single-GPU). One context per rank (one process per GPU): a device window holding a receive
- * slot per source rank ([world][max_rows][H] bf16), a return region ([max_rows][H]) and small
- * headers, shared with the other ranks through CUDA IPC. Per step, with a step counter `epoch`
- * that every rank increments identically (starting at 1):
- *   cernels_ep_dispatch  routed rows (x[perm_token[p]], p < offsets[E]) -> owners' windows
- *   cernels_ep_experts   waits for all sources, grouped GEMMs on the received rows, returns
- *                        each result row into its source's window
+ * single-GPU). One context per rank (one process per GPU): a device window holding an
+ * expert-contiguous receive region ([world * max_rows][H] bf16: every source's rows of local
+ * expert 0, then of expert 1, ...), a return region ([max_rows][H]) and small headers, shared with
+ * the other ranks through CUDA IPC. Per step:
+ *   cernels_ep_dispatch  exchanges per-expert row counts with every rank, then copies the routed
+ *                        rows (x[perm_token[p]], p < offsets[E]) to their owners' windows
+ *   cernels_ep_experts   waits for all sources, grouped GEMMs on the received rows (one group per
+ *                        local expert), returns each result row into its source's window
  *   cernels_ep_combine   waits for all results, out[t] = bf16(sum_j w[t,j] * row[inv[t,j]])
  * offsets/perm_token/inv come from cernels_moe_route over the GLOBAL expert ids (experts are
- * sharded contiguously: rank r owns [r*El, (r+1)*El)). Waits inside the kernels give up after
- * 5 s (see cernels_set_wait_limit_ns) and record a nonzero status (cernels_ep_status). */
+ * sharded contiguously: rank r owns [r*El, (r+1)*El)). `epoch` numbers the step: pass 0 to let the
+ * context count steps on the device (the three calls of a step then replay correctly from a CUDA
+ * graph), or the same nonzero, increasing value on every rank for every call of a step; do not mix
+ * the two on one context. Waits inside the kernels give up after 5 s (see
+ * cernels_set_wait_limit_ns) and record a nonzero status (cernels_ep_status). */
 #define CERNELS_EP_HANDLE_BYTES 64
 int cernels_ep_create(int32_t rank, int32_t world, int32_t hidden, int32_t local_experts, int32_t max_rows,
                       void** ctx, void* ipc_handle_out);
