@@ -37,8 +37,10 @@ constexpr int kAccStride = 256;                // TMEM column offset between the
 constexpr int kThreads = 192;
 constexpr int kTmemCols = 512;
 constexpr int kBarrierBytes = 256;
+constexpr int kStageRow = 64 * 2 + 16;              // staging row: 64 bf16 outputs + 16 B pad (no bank conflicts)
+constexpr int kStageBytes = 4 * 32 * kStageRow;     // 4 epilogue warps x 32 rows
 __host__ __device__ constexpr size_t smem_fixed(int bn) {
-  return static_cast<size_t>(kStages) * (kABytes + bn * BK * 2) + kBarrierBytes;
+  return static_cast<size_t>(kStages) * (kABytes + bn * BK * 2) + kBarrierBytes + kStageBytes;
 }
 
 constexpr float kGptOssLimit = 7.0f;
@@ -73,14 +75,6 @@ __device__ __forceinline__ TileCoord decode_tile(int t, int n_tiles, const int* 
   return c;
 }
 
-__device__ __forceinline__ void store_bf16x8(__nv_bfloat16* dst, const float* v) {
-  uint4 r;
-  __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&r);
-#pragma unroll
-  for (int i = 0; i < 4; ++i) h[i] = __floats2bfloat162_rn(v[2 * i], v[2 * i + 1]);
-  *reinterpret_cast<uint4*>(dst) = r;
-}
-
 __device__ __forceinline__ float silu(float g) { return g / (1.0f + __expf(-g)); }
 
 __device__ __forceinline__ float gptoss_glu(float gate, float up) {
@@ -106,7 +100,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint64_t* tempty_bar = bars + 2 * kStages + 2;  // [2]
   uint32_t* tmem_base_slot = reinterpret_cast<uint32_t*>(bars + 2 * kStages + 4);
   volatile int* abort_flag = reinterpret_cast<volatile int*>(tmem_base_slot + 1);
-  int* s_mt = reinterpret_cast<int*>(smem + kStages * (kABytes + kBBytes) + kBarrierBytes);  // [E + 1]
+  uint8_t* epi_stage = smem + kStages * (kABytes + kBBytes) + kBarrierBytes;       // [kStageBytes]
+  int* s_mt = reinterpret_cast<int*>(epi_stage + kStageBytes);                      // [E + 1]
 
   const int experts = args.experts;
   const int warp = threadIdx.x >> 5;
@@ -249,79 +244,100 @@ __global__ void __launch_bounds__(kThreads, 1)
       const int e = (args.b_extra != nullptr && c.expert == args.extra_group) ? 0 : c.expert % args.weight_experts;
       const int row_begin = args.offsets[c.expert];
       const int rows_e = args.group_rows ? args.group_rows[c.expert] : args.offsets[c.expert + 1] - row_begin;
-      const int local_row = c.m_tile * BM + quarter * 32 + lane;
-      const bool row_ok = local_row < rows_e;
-      const size_t grow = static_cast<size_t>(row_begin + local_row);
       const uint32_t t_row = tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + static_cast<uint32_t>(acc * kAccStride);
 
-      if constexpr (kMode == kGateUpLinear) {
-        const int F = args.out_cols;
+      // Outputs go through this warp's staging tile (32 rows x 64 bf16 columns) so that global
+      // stores write whole 128-byte row segments: 8 lanes per row, 4 rows per instruction.
+      uint8_t* stg = epi_stage + quarter * 32 * kStageRow;
+      const int tile_row0 = c.m_tile * BM + quarter * 32;  // first row of this warp, within the group
+      auto flush = [&](int col0) {
+        __syncwarp();
+#pragma unroll
+        for (int it = 0; it < 8; ++it) {
+          const int idx = it * 32 + lane;
+          const int r = idx >> 3, piece = idx & 7;
+          const int col = col0 + piece * 8;
+          if (tile_row0 + r < rows_e && col < args.out_cols) {
+            const uint4 v = *reinterpret_cast<const uint4*>(stg + r * kStageRow + piece * 16);
+            __nv_bfloat16* dst;
+            if (args.row_out) {
+              dst = args.row_out[row_begin + tile_row0 + r];
+              if (dst == nullptr) continue;
+            } else {
+              dst = args.out + static_cast<size_t>(row_begin + tile_row0 + r) * args.out_cols;
+            }
+            *reinterpret_cast<uint4*>(dst + col) = v;
+          }
+        }
+        __syncwarp();
+      };
+      auto stage8 = [&](int wcol, const float* r8) {  // 8 outputs at window column wcol of this lane's row
+        uint4 q;
+        __nv_bfloat162* h = reinterpret_cast<__nv_bfloat162*>(&q);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) h[i] = __floats2bfloat162_rn(r8[2 * i], r8[2 * i + 1]);
+        *reinterpret_cast<uint4*>(stg + lane * kStageRow + wcol * 2) = q;
+      };
+      // Per 32-column TMEM chunk: LINEAR gate/up and down produce 32 outputs, gpt-oss gate/up 16;
+      // a window of 64 outputs is flushed once full, the last one after the accumulator is
+      // released to the MMA warp.
+      constexpr int kOutPerChunk = kMode == kGateUpGptOss ? 16 : 32;
+      constexpr int kChunks = kMode == kGateUpLinear ? 4 : BN / 32;
+      constexpr int kChunksPerWindow = 64 / kOutPerChunk;
+      const int out0 = kMode == kGateUpLinear ? c.n_tile * 128 : kMode == kGateUpGptOss ? c.n_tile * BN / 2 : c.n_tile * BN;
+      const float* bias = nullptr;
+      if constexpr (kMode == kGateUpGptOss) bias = args.bias ? args.bias + static_cast<size_t>(e) * args.n : nullptr;
+      if constexpr (kMode == kDownGptOss || kMode == kDownLinear)
+        bias = args.bias ? args.bias + static_cast<size_t>(e) * args.out_cols : nullptr;
 #pragma unroll 1
-        for (int c0 = 0; c0 < 128; c0 += 32) {
+      for (int ch = 0; ch < kChunks; ++ch) {
+        const int c0 = ch * 32;
+        const int wbase = (ch % kChunksPerWindow) * kOutPerChunk;  // window column of this chunk's first output
+        if constexpr (kMode == kGateUpLinear) {
           float g[32], u[32];
           tmem_ld_32x32b_x32(t_row + c0, g);
           tmem_ld_32x32b_x32(t_row + 128 + c0, u);
-          const int col = c.n_tile * 128 + c0;
-          if (row_ok) {
 #pragma unroll
-            for (int v = 0; v < 4; ++v) {
-              if (col + 8 * v < F) {
-                float r[8];
+          for (int v = 0; v < 4; ++v) {
+            float r[8];
 #pragma unroll
-                for (int i = 0; i < 8; ++i) r[i] = silu(g[8 * v + i]) * u[8 * v + i];
-                store_bf16x8(args.out + grow * F + col + 8 * v, r);
-              }
-            }
+            for (int i = 0; i < 8; ++i) r[i] = silu(g[8 * v + i]) * u[8 * v + i];
+            stage8(wbase + 8 * v, r);
           }
-        }
-      } else if constexpr (kMode == kGateUpGptOss) {
-        const int F = args.out_cols;
-        const int two_f = args.n;
-        const float* bias = args.bias ? args.bias + static_cast<size_t>(e) * two_f : nullptr;
-#pragma unroll 1
-        for (int c0 = 0; c0 < BN; c0 += 32) {
+        } else if constexpr (kMode == kGateUpGptOss) {
           float a[32];
           tmem_ld_32x32b_x32(t_row + c0, a);
           const int wcol = c.n_tile * BN + c0;  // weight column (even = gate, odd = up)
           if (bias) {
 #pragma unroll
-            for (int i = 0; i < 32; ++i) a[i] += (wcol + i < two_f) ? __ldg(bias + wcol + i) : 0.f;
+            for (int i = 0; i < 32; ++i) a[i] += (wcol + i < args.n) ? __ldg(bias + wcol + i) : 0.f;
           }
-          const int gcol = wcol / 2;
-          if (row_ok) {
 #pragma unroll
-            for (int v = 0; v < 2; ++v) {
-              if (gcol + 8 * v < F) {
-                float r[8];
+          for (int v = 0; v < 2; ++v) {
+            float r[8];
 #pragma unroll
-                for (int i = 0; i < 8; ++i) r[i] = gptoss_glu(a[16 * v + 2 * i], a[16 * v + 2 * i + 1]);
-                store_bf16x8(args.out + grow * F + gcol + 8 * v, r);
-              }
-            }
+            for (int i = 0; i < 8; ++i) r[i] = gptoss_glu(a[16 * v + 2 * i], a[16 * v + 2 * i + 1]);
+            stage8(wbase + 8 * v, r);
           }
-        }
-      } else {
-        const int H = args.out_cols;
-        const float* bias = args.bias ? args.bias + static_cast<size_t>(e) * H : nullptr;
-#pragma unroll 1
-        for (int c0 = 0; c0 < BN; c0 += 32) {
+        } else {
           float a[32];
           tmem_ld_32x32b_x32(t_row + c0, a);
           const int col = c.n_tile * BN + c0;
           if (bias) {
 #pragma unroll
-            for (int i = 0; i < 32; ++i) a[i] += (col + i < H) ? __ldg(bias + col + i) : 0.f;
+            for (int i = 0; i < 32; ++i) a[i] += (col + i < args.out_cols) ? __ldg(bias + col + i) : 0.f;
           }
-          if (row_ok) {
 #pragma unroll
-            for (int v = 0; v < 4; ++v)
-              if (col + 8 * v < H) store_bf16x8(args.out + grow * H + col + 8 * v, a + 8 * v);
-          }
+          for (int v = 0; v < 4; ++v) stage8(wbase + 8 * v, a + 8 * v);
         }
+        if ((ch + 1) % kChunksPerWindow == 0 && ch + 1 < kChunks)
+          flush(out0 + (ch / kChunksPerWindow) * 64);
       }
+      // every TMEM read of this accumulator is done: hand it back, then write the last window
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty_bar[acc]);
+      flush(out0 + ((kChunks - 1) / kChunksPerWindow) * 64);
     }
   }
 

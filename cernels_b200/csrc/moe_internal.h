@@ -120,6 +120,10 @@ struct GroupedGemmArgs {
   // from b_extra (one slab, same layout as b) instead of b. Unused when b_extra is null.
   const __nv_bfloat16* b_extra;
   int extra_group;
+  // Optional per-row output rows (indexed like the rows of a): when set, row r's outputs go to
+  // row_out[r] (any device-visible address, a peer GPU's included; null = not written) instead
+  // of out + r * out_cols.
+  __nv_bfloat16* const* row_out;
 };
 
 enum GemmMode : int {
