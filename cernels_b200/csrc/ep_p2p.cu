@@ -18,9 +18,10 @@
 //   ep_segments  destination: waits for data_epoch == e from every source, builds the
 //                grouped-GEMM tables (one group per local expert, no partial tiles between
 //                sources) and the per-source prefix tables of the return
-//   2 x grouped_gemm_kernel on recv (tcgen05/TMA, in place)
-//   ep_return    destination: writes each result row into its source's back[seg_start + i],
-//                interleaved over sources, then release-stores s.hdr[me].result_epoch = e
+//   ep_rowmap    destination: the return address (source's back row) of every received row
+//   2 x grouped_gemm_kernel on recv (tcgen05/TMA, in place); the down GEMM's epilogue stores
+//                each result row straight into its source's back region over NVLink
+//   ep_results   destination: release-stores s.hdr[me].result_epoch = e for every source
 //   ep_combine   source: waits (acquire, bounded) for result_epoch == e from every destination,
 //                out[t] = bf16(sum_j w[t, j] * back[inv[t, j]]) in slot order
 // A rank starts step e+1 only after its combine of step e saw every destination's results,
@@ -306,43 +307,42 @@ __global__ void __launch_bounds__(1024) ep_segments_kernel(uint8_t* __restrict__
   }
 }
 
-// Destination: every result row back to its source's return region, rows interleaved over
-// sources starting at rank + 1. Source s's segment is ordered by expert; its row i of expert e
-// sits at receive row run_start[e][s] + (i - src_prefix[s][e]).
-__global__ void __launch_bounds__(kEpThreads) ep_return_kernel(uint8_t* const* __restrict__ peers, EpGeometry g,
-                                                               const uint4* __restrict__ rows,
+// Destination, before the down GEMM: the return address of every received row. Receive row r
+// belongs to (expert e, source s): it is source s's segment row i = src_prefix[s][e] +
+// (r - run_start[e][s]), whose result goes to s.back[seg_start + i]. The down GEMM's epilogue
+// stores each result row straight there (NVLink peer stores), so no separate return pass runs.
+__global__ void __launch_bounds__(kEpThreads) ep_rowmap_kernel(uint8_t* const* __restrict__ peers, EpGeometry g,
+                                                               const int* __restrict__ offsets,
                                                                const int* __restrict__ src_prefix,
-                                                               const int* __restrict__ run_start, uint32_t epoch_arg,
-                                                               const uint32_t* epoch_dev, unsigned* __restrict__ counter) {
-  const uint32_t epoch = step_epoch(epoch_dev, epoch_arg);
+                                                               const int* __restrict__ run_start,
+                                                               __nv_bfloat16** __restrict__ row_out) {
   uint8_t* own = peers[g.rank];
   const int El = g.local_experts, R = g.world;
-  const int vec = g.hidden / 8;
-  const long long cap_rows = static_cast<long long>(R) * g.cap;
-  int max_n = 0;
-  for (int s = 0; s < R; ++s) max_n = max(max_n, src_prefix[s * (El + 1) + El]);
-  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
-  const int n_warps = (gridDim.x * blockDim.x) >> 5;
-  const long long items = static_cast<long long>(max_n) * R;
-  for (long long q = warp; q < items; q += n_warps) {
-    const int i = static_cast<int>(q / R);
-    const int s = (g.rank + 1 + static_cast<int>(q % R)) % R;
-    const int* pre = src_prefix + s * (El + 1);
-    if (i >= pre[El]) continue;
-    int a = 0, b = El - 1;
+  const int total = offsets[El];
+  for (int r = blockIdx.x * blockDim.x + threadIdx.x; r < total; r += gridDim.x * blockDim.x) {
+    int a = 0, b = El - 1;  // expert: last e with offsets[e] <= r
     while (a < b) {
       const int m = (a + b + 1) >> 1;
-      if (pre[m] <= i) a = m; else b = m - 1;
+      if (offsets[m] <= r) a = m; else b = m - 1;
     }
-    const long long src_row = static_cast<long long>(run_start[a * R + s]) + (i - pre[a]);
+    int s = R - 1;  // source: last s with run_start[a][s] <= r
+    while (s > 0 && run_start[a * R + s] > r) --s;
+    const int i = src_prefix[s * (El + 1) + a] + (r - run_start[a * R + s]);
     // headers come from another rank: clamp to the windows so a bad value cannot overrun them
     const int base = min(max(hdr_of(own, s)->seg_start, 0), g.cap);
-    if (src_row < 0 || src_row >= cap_rows || base + i >= g.cap) continue;
-    copy_row(reinterpret_cast<uint4*>(peers[s] + g.back_offset) + static_cast<size_t>(base + i) * vec,
-             rows + static_cast<size_t>(src_row) * vec, vec, lane);
+    row_out[r] = (i >= 0 && base + i < g.cap)
+                     ? reinterpret_cast<__nv_bfloat16*>(peers[s] + g.back_offset) + static_cast<size_t>(base + i) * g.hidden
+                     : nullptr;
   }
-  if (last_cta_done(counter) && threadIdx.x < R)
-    st_release_sys(&hdr_of(peers[threadIdx.x], g.rank)->result_epoch, epoch);
+}
+
+// Destination, after the down GEMM (whose threads fenced their peer stores system-wide before
+// the kernel ended): tell every source that its results for this step are in place.
+__global__ void ep_results_kernel(uint8_t* const* __restrict__ peers, EpGeometry g, uint32_t epoch_arg,
+                                  const uint32_t* epoch_dev) {
+  const uint32_t epoch = step_epoch(epoch_dev, epoch_arg);
+  __threadfence_system();
+  if (threadIdx.x < g.world) st_release_sys(&hdr_of(peers[threadIdx.x], g.rank)->result_epoch, epoch);
 }
 
 // Last kernel of a step: with the device-side epoch (argument 0), its last CTA records the step
@@ -525,7 +525,8 @@ namespace {
 // Tables of the receive side, carved out of the experts workspace.
 struct EpTables {
   int *offsets, *mtile, *src_prefix, *run_start;
-  __nv_bfloat16 *glu, *down_out;
+  __nv_bfloat16** row_out;  // [rows] return address of each received row's result
+  __nv_bfloat16* glu;
 };
 size_t ep_tables(const cernels_ep_ctx* c, int inter, uint8_t* base, EpTables* t) {
   const size_t rows = static_cast<size_t>(c->geo.world) * c->geo.cap;
@@ -541,15 +542,15 @@ size_t ep_tables(const cernels_ep_ctx* c, int inter, uint8_t* base, EpTables* t)
   uint8_t* p_mt = take((El + 1) * 4);
   uint8_t* p_pre = take(R * (El + 1) * 4);
   uint8_t* p_run = take(R * El * 4);
+  uint8_t* p_rows = take(rows * sizeof(void*));
   uint8_t* p_glu = take(rows * inter * 2);
-  uint8_t* p_down = take(rows * c->geo.hidden * 2);
   if (t) {
     t->offsets = reinterpret_cast<int*>(p_off);
     t->mtile = reinterpret_cast<int*>(p_mt);
     t->src_prefix = reinterpret_cast<int*>(p_pre);
     t->run_start = reinterpret_cast<int*>(p_run);
+    t->row_out = reinterpret_cast<__nv_bfloat16**>(p_rows);
     t->glu = reinterpret_cast<__nv_bfloat16*>(p_glu);
-    t->down_out = reinterpret_cast<__nv_bfloat16*>(p_down);
   }
   return off + 256;
 }
@@ -581,6 +582,8 @@ int cernels_ep_experts(void* ctx, const cernels_moe_shape* shape, const void* ga
 
   ep_segments_kernel<<<1, 1024, 0, stream>>>(c->window, g, epoch, c->d_counters + 3, t.offsets, t.mtile,
                                              t.src_prefix, t.run_start, c->d_status);
+  ep_rowmap_kernel<<<ep_grid(static_cast<int>(rows)), kEpThreads, 0, stream>>>(c->d_peers, g, t.offsets, t.src_prefix,
+                                                                              t.run_start, t.row_out);
   cudaError_t err = cudaGetLastError();
   if (err != cudaSuccess) return rc_of(err);
   const bool gptoss = s.layout == CERNELS_LAYOUT_GPTOSS;
@@ -605,15 +608,14 @@ int cernels_ep_experts(void* ctx, const cernels_moe_shape* shape, const void* ga
   g2.a = t.glu;
   g2.b = static_cast<const __nv_bfloat16*>(down_proj);
   g2.bias = gptoss ? down_bias : nullptr;
-  g2.out = t.down_out;
+  g2.out = nullptr;
+  g2.row_out = t.row_out;  // results straight into the sources' return regions
   g2.k = s.intermediate;
   g2.n = s.hidden;
   g2.out_cols = s.hidden;
   if ((err = launch_grouped_gemm(gptoss ? kDownGptOss : kDownLinear, g2, sms, stream)) != cudaSuccess)
     return rc_of(err);
-  ep_return_kernel<<<ep_grid(static_cast<int>(c->geo.cap)), kEpThreads, 0, stream>>>(
-      c->d_peers, g, reinterpret_cast<const uint4*>(t.down_out), t.src_prefix, t.run_start, epoch,
-      c->d_counters + 3, c->d_counters + 1);
+  ep_results_kernel<<<1, 32, 0, stream>>>(c->d_peers, g, epoch, c->d_counters + 3);
   return rc_of(cudaGetLastError());
 }
 

@@ -341,6 +341,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
   }
 
+  // Outputs written through row_out may live on another GPU: make them visible system-wide
+  // before the kernel ends, so that a flag raised by a later kernel is ordered after them.
+  if (args.row_out != nullptr) __threadfence_system();
   tc_fence_before();
   __syncthreads();
   if (warp == 1) {
