@@ -57,6 +57,7 @@ def parse_args(argv=None):
     p.add_argument("--no-cpu-baseline", action="store_true")
     p.add_argument("--graph", action="store_true", help="replay the step as a CUDA graph (decode)")
     p.add_argument("--no-configs", action="store_true", help="skip the sweep over the other configurations")
+    p.add_argument("--align", action="store_true", help="multi-GPU: barrier before each timed step (outside it)")
     return p.parse_args(argv)
 
 
@@ -191,7 +192,10 @@ def make_step(cfg, case, kind, module, world, rank):
     return (lambda xx, ii, ww: fn(xx, ii, ww, module)), [case.x, idx, w], (2 if decode else 7)
 
 
-def time_device(step, inputs, steps, warmup, flush, graph=False):
+def time_device(step, inputs, steps, warmup, flush, graph=False, align=None):
+    """CUDA-event time of `steps` calls (ms total, per-step list). `align` (multi-GPU) runs
+    before each step, outside its timed interval, so that every rank starts the step together
+    and a step's time does not include another rank's late start."""
     import torch
 
     stream = torch.cuda.current_stream()
@@ -215,6 +219,8 @@ def time_device(step, inputs, steps, warmup, flush, graph=False):
     for _ in range(steps):
         if flush is not None:
             flush.zero_()
+        if align is not None:
+            align()
         a = torch.cuda.Event(enable_timing=True)
         b = torch.cuda.Event(enable_timing=True)
         a.record(stream)
@@ -507,8 +513,12 @@ def run_ours(args):
     torch.cuda.synchronize()
     log("timed region")
     use_graph = args.graph
+    align = None
+    if world > 1 and args.align:
+        def align():
+            dist.barrier(device_ids=[local])
     with ClockSampler(local) as clocks:
-        total_ms, per = time_device(step, inputs, args.steps, warmup, flush, graph=use_graph)
+        total_ms, per = time_device(step, inputs, args.steps, warmup, flush, graph=use_graph, align=align)
     log(f"clock samples: {len(clocks.samples)} ({clocks.error})")
     torch.cuda.synchronize()
     if world > 1:
@@ -577,7 +587,8 @@ def run_ours(args):
             "config": {"workload": cfg.name, "tokens": cfg.tokens, "hidden": cfg.hidden, "experts": cfg.experts,
                        "intermediate": cfg.inter, "topk": cfg.topk, "shared_intermediate": cfg.shared_inter,
                        "parallelism": f"ep{world}" if (world > 1 and cfg.name in EP_CONFIGS) else f"replica{world}",
-                       "l2": "flushed (256 MB write) before every timed step", "graph": bool(use_graph)},
+                       "l2": "flushed (256 MB write) before every timed step", "graph": bool(use_graph),
+                       "step_barrier": align is not None},
             "roofline": roof, "cpu_baseline": cpu,
             "e2e": {"value": round(e2e_value, 1), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h, "token_chunks": e2e_chunks},

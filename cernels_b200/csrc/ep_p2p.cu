@@ -7,29 +7,37 @@
 //   recv[R*cap][H]  rows routed to this rank's experts, expert-contiguous: all sources' rows of
 //                   local expert 0 (source 0 first), then expert 1, ...
 //   back[cap][H]    expert outputs of this rank's own routed rows, written by their owners
-// One step (epoch e, all kernels on the caller's stream):
+// One step (epoch e; kernels on the caller's stream unless marked "side"):
 //   ep_counts    source, one CTA per destination d: writes its per-expert row counts into
 //                d.hdr[me], release-stores count_epoch = e, waits (acquire, bounded) until
 //                every source's counts for e are in d's window, and computes where its rows
 //                of each expert start in d's receive region
-//   ep_dispatch  source: copies its routed rows (gathered from x) to those positions, work
-//                interleaved over destinations; then — after every CTA fenced — release-stores
-//                d.hdr[me].data_epoch = e
-//   ep_segments  destination: waits for data_epoch == e from every source, builds the
-//                grouped-GEMM tables (one group per local expert, no partial tiles between
-//                sources) and the per-source prefix tables of the return
+//   ep_dispatch  (side stream) source: copies its rows for the other ranks, expert by expert,
+//                and release-stores d.hdr[me].arrived[e] = e once all its rows of (d, e) are in
+//   ep_dispatch  source: copies its rows for itself (in stream order before its GEMMs)
+//   ep_segments  destination: grouped-GEMM tables from the counts (one group per local expert,
+//                all sources' rows contiguous: no partial tiles between sources)
 //   ep_rowmap    destination: the return address (source's back row) of every received row
-//   2 x grouped_gemm_kernel on recv (tcgen05/TMA, in place); the down GEMM's epilogue stores
-//                each result row straight into its source's back region over NVLink
+//   gate/up grouped GEMM (tcgen05/TMA on recv, in place): before the first tile of expert e its
+//                producer waits (bounded) for arrived[e] == e from every other source, so the
+//                GEMMs of early experts overlap the transfer of later ones
+//   down grouped GEMM: its epilogue stores each result row straight into its source's back
+//                region over NVLink
 //   ep_results   destination: release-stores s.hdr[me].result_epoch = e for every source
-//   ep_combine   source: waits (acquire, bounded) for result_epoch == e from every destination,
+//   ep_combine   source (after joining the side stream): waits (acquire, bounded) for
+//                result_epoch == e from every destination,
 //                out[t] = bf16(sum_j w[t, j] * back[inv[t, j]]) in slot order
+// The side-stream copy kernel waits for nothing, and its CTAs fit beside a resident GEMM CTA
+// (little shared memory, 256 threads), so the GEMMs that wait on other ranks' copies never
+// keep this rank's copies from running.
 // A rank starts step e+1 only after its combine of step e saw every destination's results,
 // and a destination signals results only after its GEMMs finished reading recv, so no slot
 // or header is overwritten while in use. Loads and stores are plain accesses (no TMA and no
 // multicast on peer memory). Every wait gives up after a limit (5 s unless
 // cernels_set_wait_limit_ns set another) and records a status.
 #include <cstdio>
+#include <cstddef>
+#include <cstdlib>
 #include <cstring>
 
 #include "moe_internal.h"
@@ -48,8 +56,8 @@ struct __align__(256) EpHeader {
   int32_t seg_start;                   // first routed row of this segment at the source
   int32_t n_rows;                      // rows in the segment
   uint32_t count_epoch;                // counts above are those of this step (written by the source)
-  uint32_t data_epoch;                 // written by the source (destination's window)
   uint32_t result_epoch;               // written by the destination (source's window)
+  uint32_t arrived[kEpMaxLocalExperts];  // arrived[e] == epoch: all of this source's rows of expert e are in
 };
 
 __device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
@@ -94,7 +102,7 @@ __device__ __forceinline__ void copy_row(uint4* __restrict__ dst, const uint4* _
 #pragma unroll
     for (int j = 0; j < 8; ++j) {
       const int v = v0 + j * 32 + lane;
-      if (v < vec) dst[v] = r[j];
+      if (v < vec) __stcs(dst + v, r[j]);  // streaming: the copy is not re-read from this L2
     }
   }
 }
@@ -161,8 +169,9 @@ __device__ int block_exclusive_scan(int v, int* warp_tot, int* total) {
 __global__ void __launch_bounds__(kEpThreads) ep_counts_kernel(uint8_t* const* __restrict__ peers, EpGeometry g,
                                                                const int* __restrict__ offsets, uint32_t epoch_arg,
                                                                const uint32_t* epoch_dev, int* __restrict__ dest_off,
-                                                               int* status) {
+                                                               int* __restrict__ done, int* status) {
   const uint32_t epoch = step_epoch(epoch_dev, epoch_arg);
+  for (int e = threadIdx.x; e < g.local_experts; e += blockDim.x) done[blockIdx.x * kEpMaxLocalExperts + e] = 0;
   __shared__ int cnt[kEpMaxLocalExperts];  // per expert: rows from all sources
   __shared__ int before[kEpMaxLocalExperts];  // per expert: rows from sources < me
   __shared__ int warp_tot[33];
@@ -205,50 +214,86 @@ __global__ void __launch_bounds__(kEpThreads) ep_counts_kernel(uint8_t* const* _
 }
 
 // Step 2: copy every routed row x[perm_token[p]] to its slot in its owner's receive region.
-// Work items are interleaved over destinations, starting at rank + 1, so the sources do not
-// all write to the same destination at the same time.
+// `remote` selects the destinations: every other rank (run on a side stream, concurrently with
+// the owner-side GEMMs that consume the rows) or this rank alone (in stream order before them).
+// Work is ordered by local expert, so that every destination receives all of expert 0's rows
+// first, then expert 1's, ...; inside an expert it is interleaved over destinations starting at
+// rank + 1. When the last row of (destination d, expert e) has been written (a per-(d, e) row
+// counter, after a system-scope fence by the writing warp), d.hdr[me].arrived[e] is
+// release-stored with the epoch; the owner's GEMM waits on these flags per expert.
 __global__ void __launch_bounds__(kEpThreads) ep_dispatch_kernel(uint8_t* const* __restrict__ peers, EpGeometry g,
                                                                  const uint4* __restrict__ x,
                                                                  const int* __restrict__ perm_token,
                                                                  const int* __restrict__ offsets,
                                                                  const int* __restrict__ dest_off, uint32_t epoch_arg,
-                                                                 const uint32_t* epoch_dev, unsigned* __restrict__ counter,
-                                                                 int* status) {
+                                                                 const uint32_t* epoch_dev, int* __restrict__ done,
+                                                                 int remote, int* status) {
+  __shared__ int item_prefix[kEpMaxLocalExperts + 1];
+  __shared__ int warp_tot[33];
   const uint32_t epoch = step_epoch(epoch_dev, epoch_arg);
   const int El = g.local_experts, R = g.world;
-  int max_n = 0;
-  for (int d = 0; d < R; ++d) max_n = max(max_n, offsets[(d + 1) * El] - offsets[d * El]);
+  const int nd = remote ? R - 1 : 1;  // destinations served
+  // items of expert e: (most rows any served destination gets of e) x nd
+  int carry = 0;
+  for (int e0 = 0; e0 < El; e0 += blockDim.x) {
+    const int e = e0 + threadIdx.x;
+    int items = 0;
+    if (e < El && nd > 0) {
+      int mx = 0;
+      for (int j = 0; j < nd; ++j) {
+        const int d = remote ? (g.rank + 1 + j) % R : g.rank;
+        mx = max(mx, offsets[d * El + e + 1] - offsets[d * El + e]);
+      }
+      items = mx * nd;
+    }
+    int total = 0;
+    const int excl = block_exclusive_scan(items, warp_tot, &total);
+    if (e < El) item_prefix[e] = carry + excl;
+    carry += total;
+  }
+  if (threadIdx.x == 0) item_prefix[El] = carry;
+  __syncthreads();
   const int vec = g.hidden / 8;
   const long long cap_rows = static_cast<long long>(R) * g.cap;
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5, lane = threadIdx.x & 31;
   const int n_warps = (gridDim.x * blockDim.x) >> 5;
-  const long long items = static_cast<long long>(max_n) * R;
-  for (long long q = warp; q < items; q += n_warps) {
-    const int i = static_cast<int>(q / R);
-    const int d = (g.rank + 1 + static_cast<int>(q % R)) % R;
-    const int lo = offsets[d * El];
-    if (i >= offsets[(d + 1) * El] - lo) continue;
-    const int p = lo + i;
-    // local expert of row p: last e with offsets[d*El + e] <= p
-    int a = 0, b = El - 1;
-    while (a < b) {
-      const int m = (a + b + 1) >> 1;
-      if (offsets[d * El + m] <= p) a = m; else b = m - 1;
+  for (int q = warp; q < carry; q += n_warps) {
+    int e = 0, hi = El - 1;  // expert: last e with item_prefix[e] <= q
+    while (e < hi) {
+      const int m = (e + hi + 1) >> 1;
+      if (item_prefix[m] <= q) e = m; else hi = m - 1;
     }
-    const long long dst_row = static_cast<long long>(dest_off[d * kEpMaxLocalExperts + a]) + (p - offsets[d * El + a]);
-    if (dst_row < 0 || dst_row >= cap_rows) {  // cannot happen with consistent counts; never overrun
-      if (lane == 0) atomicCAS(status, 0, kStatusTimeoutOther);
-      continue;
+    const int r = q - item_prefix[e];
+    const int i = r / nd;
+    const int d = remote ? (g.rank + 1 + r % nd) % R : g.rank;
+    const int lo = offsets[d * El + e];
+    const int n_de = offsets[d * El + e + 1] - lo;
+    if (i >= n_de) continue;
+    const long long dst_row = static_cast<long long>(dest_off[d * kEpMaxLocalExperts + e]) + i;
+    if (dst_row >= 0 && dst_row < cap_rows) {  // cannot fail with consistent counts; never overrun
+      copy_row(reinterpret_cast<uint4*>(peers[d] + g.recv_offset) + static_cast<size_t>(dst_row) * vec,
+               x + static_cast<size_t>(perm_token[lo + i]) * vec, vec, lane);
+    } else if (lane == 0) {
+      atomicCAS(status, 0, kStatusTimeoutOther);
     }
-    copy_row(reinterpret_cast<uint4*>(peers[d] + g.recv_offset) + static_cast<size_t>(dst_row) * vec,
-             x + static_cast<size_t>(perm_token[p]) * vec, vec, lane);
+    if (remote) {
+      __threadfence_system();
+      __syncwarp();
+      if (lane == 0 && atomicAdd(&done[d * kEpMaxLocalExperts + e], 1) == n_de - 1) {
+        __threadfence_system();
+        st_release_sys(&hdr_of(peers[d], g.rank)->arrived[e], epoch);
+      }
+    }
   }
-  if (last_cta_done(counter) && threadIdx.x < R)
-    st_release_sys(&hdr_of(peers[threadIdx.x], g.rank)->data_epoch, epoch);
+  // (destination, expert) pairs with no rows at all are complete from the start
+  if (remote && blockIdx.x == 0)
+    for (int idx = threadIdx.x; idx < nd * El; idx += blockDim.x) {
+      const int d = (g.rank + 1 + idx / El) % R, e = idx % El;
+      if (offsets[d * El + e + 1] == offsets[d * El + e]) st_release_sys(&hdr_of(peers[d], g.rank)->arrived[e], epoch);
+    }
 }
 
-// One CTA of 1024 threads at the destination: wait for every source, then the grouped-GEMM
-// tables (group = local expert, rows of all sources contiguous) and, per source, the prefix of
+// One CTA of 1024 threads at the destination: the grouped-GEMM tables (group = local expert, rows of all sources contiguous) and, per source, the prefix of
 // its segment by expert (for the return).
 //   offsets[e], mtile_offsets[e]  (El + 1 entries)
 //   src_prefix[s][e]              rows of source s's segment before expert e (El + 1 entries)
@@ -264,10 +309,11 @@ __global__ void __launch_bounds__(1024) ep_segments_kernel(uint8_t* __restrict__
   const int El = g.local_experts, R = g.world;
   if (threadIdx.x == 0) ok = 1;
   __syncthreads();
+  // the counts of this step are in place (ep_counts waited for them); the rows may still be on
+  // their way: the GEMM waits for them per expert
   if (threadIdx.x < R)
-    if (!wait_epoch(&hdr_of(window, threadIdx.x)->data_epoch, epoch, status, kStatusTimeoutOther, g.wait_ns)) ok = 0;
+    if (!wait_epoch(&hdr_of(window, threadIdx.x)->count_epoch, epoch, status, kStatusTimeoutOther, g.wait_ns)) ok = 0;
   __syncthreads();
-  fence_proxy_async_global();  // peer-written rows are read next by TMA (async proxy)
   const long long cap_rows = static_cast<long long>(R) * g.cap;
   int carry_rows = 0, carry_tiles = 0;
   for (int e0 = 0; e0 < El; e0 += blockDim.x) {
@@ -404,6 +450,9 @@ struct cernels_ep_ctx {
   unsigned* d_counters;  // [0] dispatch, [1] return, [2] combine, [3] last completed epoch
   int* d_status;
   int* d_dest_off;       // [kEpMaxRanks][kEpMaxLocalExperts] this rank's write offsets per destination
+  int* d_done;           // [kEpMaxRanks][kEpMaxLocalExperts] rows written per (destination, expert)
+  cudaStream_t side;     // remote dispatch, concurrent with the owner-side work of the step
+  cudaEvent_t ev_counts, ev_dispatched;
   bool connected;
 };
 
@@ -422,10 +471,17 @@ EpGeometry geo_now(const cernels_ep_ctx* c) {
   return g;
 }
 
+// CTAs of a row-copy kernel: 8 warps per CTA, a row per warp, at most `per_sm` CTAs per SM
+// (CERNELS_EP_CTAS_PER_SM overrides the default of 4, for tuning).
 int ep_grid(int rows) {
+  static const int per_sm = [] {
+    const char* v = std::getenv("CERNELS_EP_CTAS_PER_SM");
+    const int n = v ? std::atoi(v) : 0;
+    return n > 0 ? n : 4;
+  }();
   const int sms = device_sm_count();
-  const int want = (rows + 7) / 8;  // 8 warps per CTA, a row per warp
-  return want < 1 ? 1 : (want < 2 * sms ? want : 2 * sms);
+  const int want = (rows + 7) / 8;
+  return want < 1 ? 1 : (want < per_sm * sms ? want : per_sm * sms);
 }
 
 }  // namespace
@@ -458,12 +514,20 @@ int cernels_ep_create(int32_t rank, int32_t world, int32_t hidden, int32_t local
   if (err == cudaSuccess) err = cudaMalloc(&c->d_counters, 4 * sizeof(unsigned) + sizeof(int));
   if (err == cudaSuccess) err = cudaMemset(c->d_counters, 0, 4 * sizeof(unsigned) + sizeof(int));
   if (err == cudaSuccess) err = cudaMalloc(&c->d_dest_off, sizeof(int) * kEpMaxRanks * kEpMaxLocalExperts);
+  if (err == cudaSuccess) err = cudaMalloc(&c->d_done, sizeof(int) * kEpMaxRanks * kEpMaxLocalExperts);
+  if (err == cudaSuccess) err = cudaStreamCreateWithFlags(&c->side, cudaStreamNonBlocking);
+  if (err == cudaSuccess) err = cudaEventCreateWithFlags(&c->ev_counts, cudaEventDisableTiming);
+  if (err == cudaSuccess) err = cudaEventCreateWithFlags(&c->ev_dispatched, cudaEventDisableTiming);
   if (err == cudaSuccess) err = cudaIpcGetMemHandle(reinterpret_cast<cudaIpcMemHandle_t*>(handle_out), c->window);
   if (err != cudaSuccess) {
     if (c->window) cudaFree(c->window);
     if (c->d_peers) cudaFree(c->d_peers);
     if (c->d_counters) cudaFree(c->d_counters);
     if (c->d_dest_off) cudaFree(c->d_dest_off);
+    if (c->d_done) cudaFree(c->d_done);
+    if (c->side) cudaStreamDestroy(c->side);
+    if (c->ev_counts) cudaEventDestroy(c->ev_counts);
+    if (c->ev_dispatched) cudaEventDestroy(c->ev_dispatched);
     delete c;
     return rc_of(err);
   }
@@ -500,6 +564,10 @@ int cernels_ep_destroy(void* ctx) {
   cudaFree(c->d_peers);
   cudaFree(c->d_counters);
   cudaFree(c->d_dest_off);
+  cudaFree(c->d_done);
+  cudaStreamDestroy(c->side);
+  cudaEventDestroy(c->ev_counts);
+  cudaEventDestroy(c->ev_dispatched);
   delete c;
   return CERNELS_OK;
 }
@@ -514,10 +582,25 @@ int cernels_ep_dispatch(void* ctx, const void* x, const int32_t* perm_token, con
   cudaStream_t st = static_cast<cudaStream_t>(stream);
   const EpGeometry g = geo_now(c);
   ep_counts_kernel<<<c->geo.world, kEpThreads, 0, st>>>(c->d_peers, g, offsets, epoch, c->d_counters + 3,
-                                                        c->d_dest_off, c->d_status);
-  ep_dispatch_kernel<<<ep_grid(rows), kEpThreads, 0, st>>>(c->d_peers, g, static_cast<const uint4*>(x), perm_token,
-                                                          offsets, c->d_dest_off, epoch, c->d_counters + 3,
-                                                          c->d_counters, c->d_status);
+                                                        c->d_dest_off, c->d_done, c->d_status);
+  cudaError_t err = cudaGetLastError();
+  // rows for the other ranks go out on the side stream while this rank's own rows are copied
+  // and its experts run on `stream` (cernels_ep_combine joins the side stream back)
+  if (err == cudaSuccess) err = cudaEventRecord(c->ev_counts, st);
+  if (err == cudaSuccess) err = cudaStreamWaitEvent(c->side, c->ev_counts, 0);
+  if (err != cudaSuccess) return rc_of(err);
+  static const bool overlap = [] {
+    const char* v = std::getenv("CERNELS_EP_OVERLAP");  // 0: send on `stream` first (no overlap; for A/B)
+    return !(v && v[0] == '0');
+  }();
+  if (c->geo.world > 1)
+    ep_dispatch_kernel<<<ep_grid(rows), kEpThreads, 0, overlap ? c->side : st>>>(c->d_peers, g, static_cast<const uint4*>(x),
+                                                                 perm_token, offsets, c->d_dest_off, epoch,
+                                                                 c->d_counters + 3, c->d_done, 1, c->d_status);
+  if ((err = cudaEventRecord(c->ev_dispatched, c->side)) != cudaSuccess) return rc_of(err);
+  ep_dispatch_kernel<<<ep_grid(rows / c->geo.world + 1), kEpThreads, 0, st>>>(
+      c->d_peers, g, static_cast<const uint4*>(x), perm_token, offsets, c->d_dest_off, epoch, c->d_counters + 3,
+      c->d_done, 0, c->d_status);
   return rc_of(cudaGetLastError());
 }
 
@@ -602,9 +685,17 @@ int cernels_ep_experts(void* ctx, const cernels_moe_shape* shape, const void* ga
   g1.n = 2 * s.intermediate;
   g1.out_cols = s.intermediate;
   g1.weight_experts = El;
+  // rows from other ranks may still be arriving: wait per expert for every source's flag
+  g1.ready = c->window + offsetof(EpHeader, arrived);
+  g1.ready_stride = sizeof(EpHeader);
+  g1.ready_sources = c->geo.world;
+  g1.ready_self = c->geo.rank;
+  g1.ready_epoch = epoch;
+  g1.ready_epoch_dev = c->d_counters + 3;
   if ((err = launch_grouped_gemm(gptoss ? kGateUpGptOss : kGateUpLinear, g1, sms, stream)) != cudaSuccess)
     return rc_of(err);
   GroupedGemmArgs g2 = g1;
+  g2.ready = nullptr;
   g2.a = t.glu;
   g2.b = static_cast<const __nv_bfloat16*>(down_proj);
   g2.bias = gptoss ? down_bias : nullptr;
@@ -626,6 +717,8 @@ int cernels_ep_combine(void* ctx, const int32_t* inv, const float* weights, int3
   if (tokens < 0 || topk <= 0) return CERNELS_E_INVALID_SHAPE;
   if (tokens > 0 && (!inv || !weights || !out)) return CERNELS_E_NULL;
   const int blocks = tokens > 0 ? ep_grid(tokens) : 1;
+  const cudaError_t join = cudaStreamWaitEvent(static_cast<cudaStream_t>(stream), c->ev_dispatched, 0);
+  if (join != cudaSuccess) return rc_of(join);
   ep_combine_kernel<<<blocks, kEpThreads, 0, static_cast<cudaStream_t>(stream)>>>(
       c->window, geo_now(c), epoch, c->d_counters + 3, c->d_counters + 2, inv, weights, tokens, topk,
       static_cast<uint4*>(out), c->d_status);

@@ -145,8 +145,35 @@ __global__ void __launch_bounds__(kThreads, 1)
       uint32_t phase = 0;
       bool ok = true;
       long long issued = 0;  // stages loaded so far
+      int ready_group = -1;  // group whose rows are known to have arrived
+      const uint32_t epoch = args.ready == nullptr ? 0u
+                             : args.ready_epoch ? args.ready_epoch
+                                                : *reinterpret_cast<const volatile uint32_t*>(args.ready_epoch_dev) + 1u;
       for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x) {
         const TileCoord c = decode_tile(t, n_tiles, s_mt, experts);
+        if (args.ready != nullptr && c.expert != ready_group) {
+          // rows of this group come from other GPUs: wait until every source has delivered them
+          const unsigned long long t0 = global_timer_ns();
+          for (int src = 0; src < args.ready_sources && ok; ++src) {
+            if (src == args.ready_self) continue;
+            const uint32_t* flag =
+                reinterpret_cast<const uint32_t*>(args.ready + src * args.ready_stride + 4 * static_cast<size_t>(c.expert));
+            uint32_t v;
+            while (true) {
+              asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(flag) : "memory");
+              if (v == epoch) break;
+              if (*abort_flag || global_timer_ns() - t0 > args.wait_ns) {
+                if (args.status) atomicCAS(args.status, 0, kStatusTimeoutProducer);
+                *abort_flag = 1;
+                ok = false;
+                break;
+              }
+            }
+          }
+          if (!ok) break;
+          fence_proxy_async_global();  // the peer-written rows are read next by TMA
+          ready_group = c.expert;
+        }
         const int row0 = args.offsets[c.expert] + c.m_tile * BM;
         const bool extra = args.b_extra != nullptr && c.expert == args.extra_group;
         const CUtensorMap* bmap = extra ? &tmap_b_extra : &tmap_b;

@@ -124,6 +124,15 @@ struct GroupedGemmArgs {
   // row_out[r] (any device-visible address, a peer GPU's included; null = not written) instead
   // of out + r * out_cols.
   __nv_bfloat16* const* row_out;
+  // Optional arrival wait (expert parallelism): before loading the first tile of group g, the
+  // producer waits (bounded) until the 32-bit flag at ready + s * ready_stride + 4 * g equals
+  // the step's epoch for every source s != ready_self (ready_epoch, or *ready_epoch_dev + 1 when
+  // ready_epoch is 0). Null: no wait.
+  const uint8_t* ready;
+  size_t ready_stride;
+  int ready_sources, ready_self;
+  uint32_t ready_epoch;
+  const uint32_t* ready_epoch_dev;
 };
 
 enum GemmMode : int {
