@@ -559,6 +559,11 @@ def run_ours(args):
         med = torch.tensor([statistics.median(r[n] for r in rows) for n in names], device=device)
         dist.all_reduce(med, op=dist.ReduceOp.MAX)
         phases = {n: round(float(v), 4) for n, v in zip(names, med.tolist())}
+    ep_extra = None
+    if world > 1 and cfg.name == "gpt_oss_20b" and not args.no_configs:
+        # the other expert-parallel configuration (qwen3_next: 512 experts, shared expert inside
+        # the EP step), timed the same way at this N
+        ep_extra = measure_ep_config("qwen3_next", device, rank, world, min(args.steps, 10), flush, dist)
     tokens = cfg.tokens
     ms_per_step = total_ms / args.steps
     value = tokens * args.steps / (total_ms / 1e3)
@@ -598,6 +603,7 @@ def run_ours(args):
             "op_roofline_ms": round(op_roofline_ms(cfg, case), 4),
             "configs": configs,
             "ep_phases_ms": phases,
+            "ep_configs": ep_extra,
         }
         print(json.dumps(line), flush=True)
     if world > 1:
@@ -675,6 +681,41 @@ def measure_configs(steps, device):
     out["method"] = ("CUDA events on the launch stream, 256 MB L2 flush before every timed step, "
                      f"{steps} timed steps after 3 warm-up; decode entries replayed as CUDA graphs")
     return out
+
+
+def measure_ep_config(name, device, rank, world, steps, flush, dist):
+    """ms/step (max over ranks), tokens/s and per-phase times of one more EP configuration."""
+    import torch
+
+    from cernels_b200.configs import CONFIGS, make_case
+    from cernels_b200.hf_modules import build_module
+
+    try:
+        cfg = CONFIGS[name]
+        case = make_case(cfg, device=device)
+        kind, module = build_module(case, device=device)
+        step, inputs, _ = make_step(cfg, case, kind, module, world, rank)
+        dist.barrier()
+        total_ms, _ = time_device(step, inputs, steps, 3, flush)
+        t = torch.tensor([total_ms], device=device)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        ms = float(t.item()) / steps
+        planner = step.planner
+        rows = []
+        for _ in range(3):
+            flush.zero_()
+            planner.timing = []
+            step(*inputs)
+            rows.append(planner.phase_ms())
+        planner.timing = None
+        names = list(rows[0].keys())
+        med = torch.tensor([statistics.median(r[n] for r in rows) for n in names], device=device)
+        dist.all_reduce(med, op=dist.ReduceOp.MAX)
+        return {name: {"ms_per_step": round(ms, 4), "tokens_per_s": round(cfg.tokens / (ms / 1e3), 1),
+                       "tokens": cfg.tokens, "scaling": "strong", "shared_expert": "inside the EP step",
+                       "phases_ms": {n: round(float(v), 4) for n, v in zip(names, med.tolist())}}}
+    except Exception as e:  # keep the headline line
+        return {name: {"error": f"{type(e).__name__}: {e}"}}
 
 
 def op_roofline_ms(cfg, case):

@@ -53,13 +53,14 @@ PROTOTYPES = {
                                       _VP]),
     "cernels_router_topk": (ctypes.c_int, [_VP, _I32, _I32, _I32, _I32, _I32, _I32, _I32, _VP, _VP, _VP]),
     "cernels_moe_experts_shared": (ctypes.c_int, [_SHAPE_P, _VP, _VP, _VP, _VP, _VP, _VP, _VP, _VP, _VP, _SZ, _VP]),
-    "cernels_ep_create": (ctypes.c_int, [_I32, _I32, _I32, _I32, _I32, ctypes.POINTER(_VP), _VP]),
+    "cernels_ep_create": (ctypes.c_int, [_I32, _I32, _I32, _I32, _I32, _I32, ctypes.POINTER(_VP), _VP]),
     "cernels_ep_connect": (ctypes.c_int, [_VP, ctypes.c_char_p]),
     "cernels_ep_destroy": (ctypes.c_int, [_VP]),
-    "cernels_ep_dispatch": (ctypes.c_int, [_VP, _VP, _VP, _VP, _I32, ctypes.c_uint32, _VP]),
+    "cernels_ep_dispatch": (ctypes.c_int, [_VP, _VP, _VP, _VP, _I32, _I32, ctypes.c_uint32, _VP]),
     "cernels_ep_experts_workspace_bytes": (ctypes.c_int, [_VP, _SHAPE_P, ctypes.POINTER(_SZ)]),
-    "cernels_ep_experts": (ctypes.c_int, [_VP, _SHAPE_P, _VP, _VP, _VP, _VP, ctypes.c_uint32, _VP, _SZ, _VP]),
-    "cernels_ep_combine": (ctypes.c_int, [_VP, _VP, _VP, _I32, _I32, _VP, ctypes.c_uint32, _VP]),
+    "cernels_ep_experts": (ctypes.c_int, [_VP, _SHAPE_P, _VP, _VP, _VP, _VP, _VP, _VP, _I32, ctypes.c_uint32, _VP,
+                                          _SZ, _VP]),
+    "cernels_ep_combine": (ctypes.c_int, [_VP, _VP, _VP, _I32, _I32, _I32, _VP, ctypes.c_uint32, _VP]),
     "cernels_ep_status": (ctypes.c_int, [_VP, ctypes.POINTER(ctypes.c_int)]),
     "cernels_moe_route": (ctypes.c_int, [_SHAPE_P, _VP, _VP, _VP, _VP, _VP, _VP, _VP, _SZ, _VP]),
     "cernels_moe_gather": (ctypes.c_int, [_VP, _VP, _I32, _I32, _VP, _VP]),

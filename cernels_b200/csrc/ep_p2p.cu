@@ -113,6 +113,7 @@ __device__ __forceinline__ EpHeader* hdr_of(uint8_t* window, int peer) {
 
 struct EpGeometry {
   int rank, world, local_experts, cap, hidden;
+  int shared_cap;  // rows reserved after the routed ones for an always-on local (shared) expert
   size_t recv_offset, back_offset;
   unsigned long long wait_ns;  // limit of each bounded wait
 };
@@ -227,7 +228,7 @@ __global__ void __launch_bounds__(kEpThreads) ep_dispatch_kernel(uint8_t* const*
                                                                  const int* __restrict__ offsets,
                                                                  const int* __restrict__ dest_off, uint32_t epoch_arg,
                                                                  const uint32_t* epoch_dev, int* __restrict__ done,
-                                                                 int remote, int* status) {
+                                                                 int remote, int shared_tokens, int* status) {
   __shared__ int item_prefix[kEpMaxLocalExperts + 1];
   __shared__ int warp_tot[33];
   const uint32_t epoch = step_epoch(epoch_dev, epoch_arg);
@@ -285,6 +286,11 @@ __global__ void __launch_bounds__(kEpThreads) ep_dispatch_kernel(uint8_t* const*
       }
     }
   }
+  // this rank's own rows for its shared expert: x[t] -> recv[world * cap + t]
+  if (!remote)
+    for (int t = warp; t < min(shared_tokens, g.shared_cap); t += n_warps)
+      copy_row(reinterpret_cast<uint4*>(peers[g.rank] + g.recv_offset) + (cap_rows + t) * vec,
+               x + static_cast<size_t>(t) * vec, vec, lane);
   // (destination, expert) pairs with no rows at all are complete from the start
   if (remote && blockIdx.x == 0)
     for (int idx = threadIdx.x; idx < nd * El; idx += blockDim.x) {
@@ -300,9 +306,10 @@ __global__ void __launch_bounds__(kEpThreads) ep_dispatch_kernel(uint8_t* const*
 //   run_start[e][s]               first receive row of source s's rows of expert e
 __global__ void __launch_bounds__(1024) ep_segments_kernel(uint8_t* __restrict__ window, EpGeometry g,
                                                            uint32_t epoch_arg, const uint32_t* epoch_dev,
-                                                           int* __restrict__ offsets, int* __restrict__ mtile_offsets,
+                                                           int* __restrict__ offsets, int* __restrict__ group_rows,
+                                                           int* __restrict__ mtile_offsets,
                                                            int* __restrict__ src_prefix, int* __restrict__ run_start,
-                                                           int* status) {
+                                                           int shared_tokens, int* status) {
   const uint32_t epoch = step_epoch(epoch_dev, epoch_arg);
   __shared__ int ok;
   __shared__ int warp_tot[33];
@@ -329,6 +336,7 @@ __global__ void __launch_bounds__(1024) ep_segments_kernel(uint8_t* __restrict__
       // clamp so that a bad header can never make the GEMM read past the receive region
       const long long start = min(static_cast<long long>(carry_rows + row_excl), cap_rows);
       offsets[e] = static_cast<int>(start);
+      group_rows[e] = static_cast<int>(min(static_cast<long long>(rows), cap_rows - start));
       mtile_offsets[e] = carry_tiles + tile_excl;
       int r = static_cast<int>(start);
       for (int s = 0; s < R; ++s) {
@@ -348,8 +356,12 @@ __global__ void __launch_bounds__(1024) ep_segments_kernel(uint8_t* __restrict__
     src_prefix[s * (El + 1) + El] = acc;
   }
   if (threadIdx.x == 0) {
-    offsets[El] = static_cast<int>(min(static_cast<long long>(carry_rows), cap_rows));
+    // group El, when present: this rank's own tokens for its shared expert, after the routed capacity
+    const int sh = min(shared_tokens, g.shared_cap);
+    offsets[El] = static_cast<int>(cap_rows);
+    group_rows[El] = sh;
     mtile_offsets[El] = carry_tiles;
+    mtile_offsets[El + 1] = carry_tiles + (sh + kBlockM - 1) / kBlockM;
   }
 }
 
@@ -359,12 +371,19 @@ __global__ void __launch_bounds__(1024) ep_segments_kernel(uint8_t* __restrict__
 // stores each result row straight there (NVLink peer stores), so no separate return pass runs.
 __global__ void __launch_bounds__(kEpThreads) ep_rowmap_kernel(uint8_t* const* __restrict__ peers, EpGeometry g,
                                                                const int* __restrict__ offsets,
+                                                               const int* __restrict__ group_rows,
                                                                const int* __restrict__ src_prefix,
                                                                const int* __restrict__ run_start,
                                                                __nv_bfloat16** __restrict__ row_out) {
   uint8_t* own = peers[g.rank];
   const int El = g.local_experts, R = g.world;
-  const int total = offsets[El];
+  const int total = offsets[El - 1] + group_rows[El - 1];  // routed rows (contiguous from 0)
+  // shared-expert rows: results of this rank's own tokens go to back[cap + t]
+  const long long cap_rows = static_cast<long long>(R) * g.cap;
+  for (int t = blockIdx.x * blockDim.x + threadIdx.x; t < group_rows[El] && g.shared_cap > 0;
+       t += gridDim.x * blockDim.x)
+    row_out[cap_rows + t] = reinterpret_cast<__nv_bfloat16*>(own + g.back_offset) +
+                            static_cast<size_t>(g.cap + t) * g.hidden;
   for (int r = blockIdx.x * blockDim.x + threadIdx.x; r < total; r += gridDim.x * blockDim.x) {
     int a = 0, b = El - 1;  // expert: last e with offsets[e] <= r
     while (a < b) {
@@ -398,7 +417,8 @@ __global__ void __launch_bounds__(kEpThreads) ep_combine_kernel(uint8_t* __restr
                                                                 unsigned* __restrict__ counter,
                                                                 const int* __restrict__ inv,
                                                                 const float* __restrict__ weights, int tokens,
-                                                                int topk, uint4* __restrict__ out, int* status) {
+                                                                int topk, int shared, uint4* __restrict__ out,
+                                                                int* status) {
   const uint32_t epoch = step_epoch(epoch_dev, epoch_arg);
   __shared__ int ok;
   if (threadIdx.x == 0) ok = 1;
@@ -413,7 +433,8 @@ __global__ void __launch_bounds__(kEpThreads) ep_combine_kernel(uint8_t* __restr
     for (int v = threadIdx.x & 31; v < vec; v += 32) {
       float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
       for (int j = 0; j < topk && ok; ++j) {
-        const int p = inv[static_cast<size_t>(t) * topk + j];
+        // with a shared expert, the last slot's row is this token's shared-expert result
+        const int p = (shared && j == topk - 1) ? g.cap + t : inv[static_cast<size_t>(t) * topk + j];
         if (p < 0) continue;
         const uint4 r = __ldcv(back + static_cast<size_t>(p) * vec + v);
         const float w = weights[static_cast<size_t>(t) * topk + j];
@@ -489,10 +510,11 @@ int ep_grid(int rows) {
 extern "C" {
 
 int cernels_ep_create(int32_t rank, int32_t world, int32_t hidden, int32_t local_experts, int32_t max_rows,
-                      void** ctx_out, void* handle_out) {
+                      int32_t shared_rows, void** ctx_out, void* handle_out) {
   if (!ctx_out || !handle_out) return CERNELS_E_NULL;
   if (world < 1 || world > kEpMaxRanks || rank < 0 || rank >= world) return CERNELS_E_INVALID_SHAPE;
-  if (hidden <= 0 || hidden % 8 || local_experts <= 0 || local_experts > kEpMaxLocalExperts || max_rows <= 0)
+  if (hidden <= 0 || hidden % 8 || local_experts <= 0 || local_experts > kEpMaxLocalExperts || max_rows <= 0 ||
+      shared_rows < 0)
     return CERNELS_E_INVALID_SHAPE;
   if (world * local_experts > kMaxExperts) return CERNELS_E_UNSUPPORTED;
   auto* c = new cernels_ep_ctx();
@@ -506,8 +528,9 @@ int cernels_ep_create(int32_t rank, int32_t world, int32_t hidden, int32_t local
   const size_t hdr = align_up(sizeof(EpHeader) * world, 1024);
   const size_t row = static_cast<size_t>(hidden) * 2;
   c->geo.recv_offset = hdr;
-  c->geo.back_offset = align_up(hdr + static_cast<size_t>(world) * max_rows * row, 1024);
-  c->window_bytes = c->geo.back_offset + static_cast<size_t>(max_rows) * row;
+  c->geo.shared_cap = shared_rows;
+  c->geo.back_offset = align_up(hdr + (static_cast<size_t>(world) * max_rows + shared_rows) * row, 1024);
+  c->window_bytes = c->geo.back_offset + (static_cast<size_t>(max_rows) + shared_rows) * row;
   cudaError_t err = cudaMalloc(&c->window, c->window_bytes);
   if (err == cudaSuccess) err = cudaMemset(c->window, 0, c->geo.recv_offset);
   if (err == cudaSuccess) err = cudaMalloc(&c->d_peers, sizeof(uint8_t*) * kEpMaxRanks);
@@ -573,10 +596,10 @@ int cernels_ep_destroy(void* ctx) {
 }
 
 int cernels_ep_dispatch(void* ctx, const void* x, const int32_t* perm_token, const int32_t* offsets, int32_t rows,
-                        uint32_t epoch, void* stream) {
+                        int32_t shared_tokens, uint32_t epoch, void* stream) {
   auto* c = static_cast<cernels_ep_ctx*>(ctx);
   if (!c || !c->connected) return CERNELS_E_NULL;
-  if (rows > c->geo.cap) return CERNELS_E_UNSUPPORTED;
+  if (rows > c->geo.cap || shared_tokens < 0 || shared_tokens > c->geo.shared_cap) return CERNELS_E_UNSUPPORTED;
   if (rows > 0 && (!x || !perm_token || !offsets)) return CERNELS_E_NULL;
   if (x && (reinterpret_cast<uintptr_t>(x) & 15)) return CERNELS_E_ALIGNMENT;
   cudaStream_t st = static_cast<cudaStream_t>(stream);
@@ -596,23 +619,23 @@ int cernels_ep_dispatch(void* ctx, const void* x, const int32_t* perm_token, con
   if (c->geo.world > 1)
     ep_dispatch_kernel<<<ep_grid(rows), kEpThreads, 0, overlap ? c->side : st>>>(c->d_peers, g, static_cast<const uint4*>(x),
                                                                  perm_token, offsets, c->d_dest_off, epoch,
-                                                                 c->d_counters + 3, c->d_done, 1, c->d_status);
+                                                                 c->d_counters + 3, c->d_done, 1, 0, c->d_status);
   if ((err = cudaEventRecord(c->ev_dispatched, c->side)) != cudaSuccess) return rc_of(err);
-  ep_dispatch_kernel<<<ep_grid(rows / c->geo.world + 1), kEpThreads, 0, st>>>(
+  ep_dispatch_kernel<<<ep_grid(rows / c->geo.world + shared_tokens + 1), kEpThreads, 0, st>>>(
       c->d_peers, g, static_cast<const uint4*>(x), perm_token, offsets, c->d_dest_off, epoch, c->d_counters + 3,
-      c->d_done, 0, c->d_status);
+      c->d_done, 0, shared_tokens, c->d_status);
   return rc_of(cudaGetLastError());
 }
 
 namespace {
 // Tables of the receive side, carved out of the experts workspace.
 struct EpTables {
-  int *offsets, *mtile, *src_prefix, *run_start;
+  int *offsets, *group_rows, *mtile, *src_prefix, *run_start;
   __nv_bfloat16** row_out;  // [rows] return address of each received row's result
   __nv_bfloat16* glu;
 };
 size_t ep_tables(const cernels_ep_ctx* c, int inter, uint8_t* base, EpTables* t) {
-  const size_t rows = static_cast<size_t>(c->geo.world) * c->geo.cap;
+  const size_t rows = static_cast<size_t>(c->geo.world) * c->geo.cap + c->geo.shared_cap;
   const size_t El = c->geo.local_experts, R = c->geo.world;
   size_t off = 0;
   auto take = [&](size_t bytes) {
@@ -621,14 +644,16 @@ size_t ep_tables(const cernels_ep_ctx* c, int inter, uint8_t* base, EpTables* t)
     off += bytes;
     return p;
   };
-  uint8_t* p_off = take((El + 1) * 4);
-  uint8_t* p_mt = take((El + 1) * 4);
+  uint8_t* p_off = take((El + 2) * 4);
+  uint8_t* p_gr = take((El + 2) * 4);
+  uint8_t* p_mt = take((El + 2) * 4);
   uint8_t* p_pre = take(R * (El + 1) * 4);
   uint8_t* p_run = take(R * El * 4);
   uint8_t* p_rows = take(rows * sizeof(void*));
   uint8_t* p_glu = take(rows * inter * 2);
   if (t) {
     t->offsets = reinterpret_cast<int*>(p_off);
+    t->group_rows = reinterpret_cast<int*>(p_gr);
     t->mtile = reinterpret_cast<int*>(p_mt);
     t->src_prefix = reinterpret_cast<int*>(p_pre);
     t->run_start = reinterpret_cast<int*>(p_run);
@@ -647,7 +672,8 @@ int cernels_ep_experts_workspace_bytes(void* ctx, const cernels_moe_shape* shape
 }
 
 int cernels_ep_experts(void* ctx, const cernels_moe_shape* shape, const void* gate_up_proj, const float* gate_up_bias,
-                       const void* down_proj, const float* down_bias, uint32_t epoch, void* workspace,
+                       const void* down_proj, const float* down_bias, const void* shared_gate_up_proj,
+                       const void* shared_down_proj, int32_t shared_tokens, uint32_t epoch, void* workspace,
                        size_t workspace_bytes, void* stream_ptr) {
   auto* c = static_cast<cernels_ep_ctx*>(ctx);
   if (!c || !c->connected || !shape || !gate_up_proj || !down_proj || !workspace) return CERNELS_E_NULL;
@@ -656,17 +682,21 @@ int cernels_ep_experts(void* ctx, const cernels_moe_shape* shape, const void* ga
       s.intermediate % 8)
     return CERNELS_E_INVALID_SHAPE;
   if (workspace_bytes < ep_tables(c, s.intermediate, nullptr, nullptr)) return CERNELS_E_WORKSPACE;
+  const bool shared = shared_tokens > 0;
+  if (shared_tokens < 0 || shared_tokens > c->geo.shared_cap) return CERNELS_E_UNSUPPORTED;
+  if (shared && (!shared_gate_up_proj || !shared_down_proj)) return CERNELS_E_NULL;
+  if (shared && s.layout != CERNELS_LAYOUT_LINEAR) return CERNELS_E_UNSUPPORTED;
   cudaStream_t stream = static_cast<cudaStream_t>(stream_ptr);
   EpTables t;
   ep_tables(c, s.intermediate, static_cast<uint8_t*>(workspace), &t);
   const EpGeometry g = geo_now(c);
   const int El = c->geo.local_experts;
-  const size_t rows = static_cast<size_t>(c->geo.world) * c->geo.cap;
+  const size_t rows = static_cast<size_t>(c->geo.world) * c->geo.cap + c->geo.shared_cap;
 
-  ep_segments_kernel<<<1, 1024, 0, stream>>>(c->window, g, epoch, c->d_counters + 3, t.offsets, t.mtile,
-                                             t.src_prefix, t.run_start, c->d_status);
-  ep_rowmap_kernel<<<ep_grid(static_cast<int>(rows)), kEpThreads, 0, stream>>>(c->d_peers, g, t.offsets, t.src_prefix,
-                                                                              t.run_start, t.row_out);
+  ep_segments_kernel<<<1, 1024, 0, stream>>>(c->window, g, epoch, c->d_counters + 3, t.offsets, t.group_rows,
+                                             t.mtile, t.src_prefix, t.run_start, shared_tokens, c->d_status);
+  ep_rowmap_kernel<<<ep_grid(static_cast<int>(rows)), kEpThreads, 0, stream>>>(c->d_peers, g, t.offsets, t.group_rows,
+                                                                              t.src_prefix, t.run_start, t.row_out);
   cudaError_t err = cudaGetLastError();
   if (err != cudaSuccess) return rc_of(err);
   const bool gptoss = s.layout == CERNELS_LAYOUT_GPTOSS;
@@ -677,14 +707,19 @@ int cernels_ep_experts(void* ctx, const cernels_moe_shape* shape, const void* ga
   g1.bias = gptoss ? gate_up_bias : nullptr;
   g1.out = t.glu;
   g1.offsets = t.offsets;
+  g1.group_rows = t.group_rows;
   g1.mtile_offsets = t.mtile;
   g1.status = c->d_status;
   g1.rows = static_cast<int>(rows);
-  g1.experts = El;
+  g1.experts = El + (shared ? 1 : 0);  // group El: the shared expert on this rank's own tokens
   g1.k = s.hidden;
   g1.n = 2 * s.intermediate;
   g1.out_cols = s.intermediate;
   g1.weight_experts = El;
+  if (shared) {
+    g1.b_extra = static_cast<const __nv_bfloat16*>(shared_gate_up_proj);
+    g1.extra_group = El;
+  }
   // rows from other ranks may still be arriving: wait per expert for every source's flag
   g1.ready = c->window + offsetof(EpHeader, arrived);
   g1.ready_stride = sizeof(EpHeader);
@@ -698,6 +733,7 @@ int cernels_ep_experts(void* ctx, const cernels_moe_shape* shape, const void* ga
   g2.ready = nullptr;
   g2.a = t.glu;
   g2.b = static_cast<const __nv_bfloat16*>(down_proj);
+  if (shared) g2.b_extra = static_cast<const __nv_bfloat16*>(shared_down_proj);
   g2.bias = gptoss ? down_bias : nullptr;
   g2.out = nullptr;
   g2.row_out = t.row_out;  // results straight into the sources' return regions
@@ -710,18 +746,19 @@ int cernels_ep_experts(void* ctx, const cernels_moe_shape* shape, const void* ga
   return rc_of(cudaGetLastError());
 }
 
-int cernels_ep_combine(void* ctx, const int32_t* inv, const float* weights, int32_t tokens, int32_t topk, void* out,
-                       uint32_t epoch, void* stream) {
+int cernels_ep_combine(void* ctx, const int32_t* inv, const float* weights, int32_t tokens, int32_t topk,
+                       int32_t shared, void* out, uint32_t epoch, void* stream) {
   auto* c = static_cast<cernels_ep_ctx*>(ctx);
   if (!c || !c->connected) return CERNELS_E_NULL;
-  if (tokens < 0 || topk <= 0) return CERNELS_E_INVALID_SHAPE;
+  if (tokens < 0 || topk <= 0 || (shared && topk < 2)) return CERNELS_E_INVALID_SHAPE;
+  if (shared && tokens > c->geo.shared_cap) return CERNELS_E_UNSUPPORTED;
   if (tokens > 0 && (!inv || !weights || !out)) return CERNELS_E_NULL;
   const int blocks = tokens > 0 ? ep_grid(tokens) : 1;
   const cudaError_t join = cudaStreamWaitEvent(static_cast<cudaStream_t>(stream), c->ev_dispatched, 0);
   if (join != cudaSuccess) return rc_of(join);
   ep_combine_kernel<<<blocks, kEpThreads, 0, static_cast<cudaStream_t>(stream)>>>(
       c->window, geo_now(c), epoch, c->d_counters + 3, c->d_counters + 2, inv, weights, tokens, topk,
-      static_cast<uint4*>(out), c->d_status);
+      shared != 0, static_cast<uint4*>(out), c->d_status);
   return rc_of(cudaGetLastError());
 }
 

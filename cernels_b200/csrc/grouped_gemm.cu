@@ -151,7 +151,8 @@ __global__ void __launch_bounds__(kThreads, 1)
                                                 : *reinterpret_cast<const volatile uint32_t*>(args.ready_epoch_dev) + 1u;
       for (int t = blockIdx.x; t < total_tiles && ok; t += gridDim.x) {
         const TileCoord c = decode_tile(t, n_tiles, s_mt, experts);
-        if (args.ready != nullptr && c.expert != ready_group) {
+        const bool local_group = args.b_extra != nullptr && c.expert == args.extra_group;  // rows from this GPU
+        if (args.ready != nullptr && c.expert != ready_group && !local_group) {
           // rows of this group come from other GPUs: wait until every source has delivered them
           const unsigned long long t0 = global_timer_ns();
           for (int src = 0; src < args.ready_sources && ok; ++src) {

@@ -2,26 +2,27 @@
 
 The reference is single-GPU; expert parallelism is the north star's multi-GPU scheme for
 the large-token configurations (qwen3_next, gpt_oss). Rank r of R owns the contiguous
-expert slice [r*E/R, (r+1)*E/R) and the contiguous token slice of its batch. One forward:
+expert slice [r*E/R, (r+1)*E/R) and the contiguous token slice of its batch.
 
-  1. router on the local tokens (linear in cuBLAS, top-k/softmax in one kernel)
+Default transport: NVLink peer memory (``P2PTransport`` over ``cernels_ep_*``, see
+csrc/ep_p2p.cu). One forward, without any host synchronisation:
+
+  1. router on the local tokens (one tensor-core kernel: linear + top-k + softmax)
   2. routing kernel over the GLOBAL expert ids: offsets, stable permutation, inverse map
-     — rows bound for rank d are contiguous because experts are sharded contiguously
-  3. per-expert counts for each destination exchanged with all_to_all_single; one small
-     device->host copy gives the split sizes NCCL needs
-  4. gather kernel builds the send buffer (local token rows in routed order)
-  5. dispatch all_to_all_single (NCCL over NVLink) -> rows for my experts, ordered by
-     (source rank, local expert). Each destination segment is cut into C contiguous row
-     pieces and the send buffer is laid out chunk-major, so chunk c's dispatch, chunk c-1's
-     expert GEMMs and chunk c-2's return overlap (NCCL runs on its own stream)
-  6. local experts: the grouped tcgen05 GEMMs read the received rows in place — they are
-     contiguous runs per (source rank, local expert), each run one GEMM group — + bias
-  7. combine all_to_all_single back -> every row returns to its source position
-  8. combine kernel: out[t] = sum_j w[t, j] * row[inv[t, j]] in fp32, slot order
-  (qwen3_next adds its gated shared expert on the local tokens.)
+  3. per-expert row counts exchanged through the peers' windows; every rank learns where its
+     rows go in each owner's expert-contiguous receive region
+  4. rows for the other ranks copied straight into their windows on a side stream, expert by
+     expert, with a per-(rank, expert) arrival flag; this rank's own rows copied in order
+  5. owner side: grouped tcgen05 GEMMs on the received rows in place; the gate/up GEMM waits per
+     expert for the arrival flags (so it overlaps the transfer), the down GEMM's epilogue stores
+     every result row into its source's return region over NVLink
+  6. combine kernel: out[t] = sum_j w[t, j] * row[inv[t, j]] in fp32, slot order
+  qwen3_next runs its shared expert inside the same GEMMs, as one more group on the local tokens.
 
-All device work goes through a ``Backend`` (the CUDA kernels by default). Tests run the
-same exchange logic on CPU gloo ranks with a CPU backend.
+``transport="nccl"`` (and the CPU path the tests run on gloo ranks): counts and rows exchanged
+with all_to_all_single, the received rows (runs per (source rank, local expert)) through
+``cernels_moe_grouped_experts``, results returned by a second all-to-all; optional chunking
+pipelines dispatch, GEMMs and return. All device work goes through a ``Backend``.
 """
 
 from __future__ import annotations
@@ -78,7 +79,8 @@ class P2PTransport:
     """Device-side dispatch / return over NVLink peer memory (include/cernels_b200.h,
     cernels_ep_*): one IPC-shared window per rank, no NCCL and no host sync per step."""
 
-    def __init__(self, rank: int, world: int, hidden: int, local_experts: int, max_rows: int, device, group=None):
+    def __init__(self, rank: int, world: int, hidden: int, local_experts: int, max_rows: int, device, group=None,
+                 shared_rows: int = 0):
         import ctypes
 
         from . import _lib
@@ -88,14 +90,15 @@ class P2PTransport:
         self.ctx = ctypes.c_void_p()
         handle = ctypes.create_string_buffer(64)
         with torch.cuda.device(device):
-            _lib.check(lib.cernels_ep_create(rank, world, hidden, local_experts, max_rows, ctypes.byref(self.ctx),
-                                             handle), "cernels_ep_create")
+            _lib.check(lib.cernels_ep_create(rank, world, hidden, local_experts, max_rows, shared_rows,
+                                             ctypes.byref(self.ctx), handle), "cernels_ep_create")
             handles = [None] * world
             dist.all_gather_object(handles, handle.raw, group=group)
             _lib.check(lib.cernels_ep_connect(self.ctx, b"".join(handles)), "cernels_ep_connect")
         dist.barrier(group=group)
         self.device = device
         self.max_rows = max_rows
+        self.shared_rows = shared_rows
         self._ws = None  # epochs are counted on the device (epoch argument 0): steps replay from CUDA graphs
 
     def status(self) -> int:
@@ -105,32 +108,38 @@ class P2PTransport:
         self._lib.check(self._lib.load().cernels_ep_status(self.ctx, ctypes.byref(st)), "cernels_ep_status")
         return int(st.value)
 
-    def step(self, x, perm_token, offsets, inv, w, weights, shape, mark=lambda: None):
-        """dispatch -> grouped experts -> return -> combine for one batch; returns [T, H] bf16."""
+    def step(self, x, perm_token, offsets, inv, w, weights, shape, mark=lambda: None, shared=None):
+        """dispatch -> grouped experts (results stored back into the sources' windows) -> combine
+        for one batch; returns [T, H] bf16. shared = (w1 [1, 2F, H], w2 [1, H, F]): an always-on
+        expert on this rank's tokens, weighted by the last column of w."""
         import ctypes
 
         lib = self._lib.load()
         T, k = w.shape
         if T * k > self.max_rows:
             raise RuntimeError(f"expert-parallel window holds {self.max_rows} routed rows, batch has {T * k}")
+        if shared is not None and T > self.shared_rows:
+            raise RuntimeError(f"expert-parallel window holds {self.shared_rows} shared-expert rows, batch has {T}")
         layout, w1, b1, w2, b2 = weights
+        n_shared = T if shared is not None else 0
         stream = torch.cuda.current_stream(self.device).cuda_stream
         ptr = lambda t: None if t is None else t.data_ptr()  # noqa: E731
         self._lib.check(lib.cernels_ep_dispatch(self.ctx, x.data_ptr(), perm_token.data_ptr(), offsets.data_ptr(),
-                                                T * k, 0, stream), "cernels_ep_dispatch")
+                                                T * k, n_shared, 0, stream), "cernels_ep_dispatch")
         mark()
         n = ctypes.c_size_t(0)
         self._lib.check(lib.cernels_ep_experts_workspace_bytes(self.ctx, ctypes.byref(shape), ctypes.byref(n)),
                         "cernels_ep_experts_workspace_bytes")
         if self._ws is None or self._ws.numel() < n.value:
             self._ws = torch.empty(n.value, dtype=torch.uint8, device=self.device)
+        sw1, sw2 = shared if shared is not None else (None, None)
         self._lib.check(lib.cernels_ep_experts(self.ctx, ctypes.byref(shape), w1.data_ptr(), ptr(b1), w2.data_ptr(),
-                                               ptr(b2), 0, self._ws.data_ptr(), n.value, stream),
-                        "cernels_ep_experts")
+                                               ptr(b2), ptr(sw1), ptr(sw2), n_shared, 0, self._ws.data_ptr(), n.value,
+                                               stream), "cernels_ep_experts")
         mark()
         out = torch.empty(T, x.shape[1], dtype=x.dtype, device=x.device)
-        self._lib.check(lib.cernels_ep_combine(self.ctx, inv.data_ptr(), w.data_ptr(), T, k, out.data_ptr(),
-                                               0, stream), "cernels_ep_combine")
+        self._lib.check(lib.cernels_ep_combine(self.ctx, inv.data_ptr(), w.data_ptr(), T, k, int(n_shared > 0),
+                                               out.data_ptr(), 0, stream), "cernels_ep_combine")
         mark()
         return out
 
@@ -147,7 +156,8 @@ class ExpertParallelMoe:
 
     def __init__(self, experts: int, topk: int, rank: int, world: int, router: Callable, backend: Backend,
                  shared: Callable | None = None, group=None, chunks: int | None = None,
-                 local_weights: tuple | None = None, transport: str = "auto"):
+                 local_weights: tuple | None = None, transport: str = "auto",
+                 fused_shared: tuple | None = None):
         self.E = experts
         self.k = topk
         self.rank = rank
@@ -161,9 +171,14 @@ class ExpertParallelMoe:
         # (layout, w1, b1, w2, b2) of the local expert slice; needed by the peer-memory transport
         self.local_weights = local_weights
         self.transport = transport  # "p2p" (CUDA peer memory), "nccl", or "auto"
+        # (router_with_shared_slot, (shared w1, shared w2)): the peer-memory path runs the shared
+        # expert inside the EP step as one more grouped-GEMM group; the router then returns
+        # topk + 1 columns, the last one (E, shared gate weight)
+        self.fused_shared = fused_shared
         self._p2p = None
-        # router tail(1) + route(3) + dispatch(1) + segments(1) + 2 GEMMs + return(1) + combine(1); + 8 shared
-        self.launches_per_step = 10 + (8 if shared is not None else 0)
+        # router(1) + route(3) + counts(1) + 2 copies + segments(1) + rowmap(1) + 2 GEMMs + results(1)
+        # + combine(1)
+        self.launches_per_step = 13
 
     # ------------------------------------------------------------ construction
     @classmethod
@@ -201,8 +216,11 @@ class ExpertParallelMoe:
             def router(x):
                 return qn.route(x, module)
 
+            fused = None
+            if qn.fused_shared_supported(module):
+                fused = (lambda x: qn._fused_route(x, module), qn._shared_weights(module))
             return cls(E, int(module.gate.top_k), rank, world, router, backend, lambda x: qn.shared_expert(x, module),
-                       group, local_weights=local)
+                       group, local_weights=local, fused_shared=fused)
         raise ValueError(f"expert parallelism is not used for {kind}")
 
     # ------------------------------------------------------------ forward
@@ -255,27 +273,29 @@ class ExpertParallelMoe:
 
         if getattr(self, "timing", None) is not None:
             self.timing = []
+        fused = self.fused_shared
         with torch.no_grad():
             self._mark()
-            idx, w = self.router(x)
+            idx, w = (fused[0] if fused is not None else self.router)(x)
             idx = idx.to(torch.int32).contiguous()
             w = w.float().contiguous()
             self._mark()
+            # the shared slot's id E is outside [0, E): routing skips it (inv = -1)
             offsets, perm_token, _perm_weight, inv = self.backend.route(idx, w, self.E)
             self._mark()
             if self._p2p is None:
-                # window capacity: the most routed rows any rank can send (all ranks agree)
-                cap = torch.tensor([idx.numel()], dtype=torch.int64, device=x.device)
+                # window capacity: the most routed rows (and tokens) any rank has (all ranks agree)
+                cap = torch.tensor([idx.numel(), x.shape[0]], dtype=torch.int64, device=x.device)
                 dist.all_reduce(cap, op=dist.ReduceOp.MAX, group=self.group)
-                self._p2p = P2PTransport(self.rank, self.world, x.shape[1], self.E // self.world, int(cap.item()),
-                                         x.device, self.group)
+                self._p2p = P2PTransport(self.rank, self.world, x.shape[1], self.E // self.world, int(cap[0].item()),
+                                         x.device, self.group, shared_rows=int(cap[1].item()) if fused else 0)
             layout, w1, b1, w2, b2 = self.local_weights
             F = w1.shape[1] // 2 if layout == 0 else w1.shape[2] // 2
             shape = _lib.MoeShape(int(self._p2p.max_rows), int(x.shape[1]), int(self.E // self.world), int(F), 1,
                                   int(layout))
             out = self._p2p.step(x.contiguous(), perm_token, offsets, inv, w, self.local_weights, shape,
-                                 mark=self._mark)
-            if self.shared is not None:
+                                 mark=self._mark, shared=None if fused is None else fused[1])
+            if self.shared is not None and fused is None:
                 out = out + self.shared(x)
                 self._mark()
             return out

@@ -218,18 +218,27 @@ int cernels_moe_experts_decode_noalloc(const cernels_moe_shape* shape, const voi
  * the two on one context. Waits inside the kernels give up after 5 s (see
  * cernels_set_wait_limit_ns) and record a nonzero status (cernels_ep_status). */
 #define CERNELS_EP_HANDLE_BYTES 64
+/* shared_rows > 0 reserves room for an always-on shared expert (the Qwen3-Next layout): up to
+ * shared_rows of this rank's own tokens run through it inside the same grouped GEMMs, and
+ * cernels_ep_combine adds it as the last routing slot. */
 int cernels_ep_create(int32_t rank, int32_t world, int32_t hidden, int32_t local_experts, int32_t max_rows,
-                      void** ctx, void* ipc_handle_out);
+                      int32_t shared_rows, void** ctx, void* ipc_handle_out);
 int cernels_ep_connect(void* ctx, const void* ipc_handles /* world * CERNELS_EP_HANDLE_BYTES, rank order */);
 int cernels_ep_destroy(void* ctx);
+/* shared_tokens: this rank's tokens (x rows 0..shared_tokens-1) for the shared expert, or 0. */
 int cernels_ep_dispatch(void* ctx, const void* x, const int32_t* perm_token, const int32_t* offsets, int32_t rows,
-                        uint32_t epoch, void* stream);
+                        int32_t shared_tokens, uint32_t epoch, void* stream);
 int cernels_ep_experts_workspace_bytes(void* ctx, const cernels_moe_shape* shape, size_t* bytes);
+/* shared_gate_up_proj [1, 2F, H] / shared_down_proj [1, H, F] (LINEAR layout, same F) with
+ * shared_tokens > 0: the shared expert runs as one more group of the grouped GEMMs. */
 int cernels_ep_experts(void* ctx, const cernels_moe_shape* shape, const void* gate_up_proj, const float* gate_up_bias,
-                       const void* down_proj, const float* down_bias, uint32_t epoch, void* workspace,
+                       const void* down_proj, const float* down_bias, const void* shared_gate_up_proj,
+                       const void* shared_down_proj, int32_t shared_tokens, uint32_t epoch, void* workspace,
                        size_t workspace_bytes, void* stream);
-int cernels_ep_combine(void* ctx, const int32_t* inv, const float* weights, int32_t tokens, int32_t topk, void* out,
-                       uint32_t epoch, void* stream);
+/* shared != 0: slot topk - 1 of every token is its shared-expert result (its weight the gate),
+ * the other slots routed as given by inv. */
+int cernels_ep_combine(void* ctx, const int32_t* inv, const float* weights, int32_t tokens, int32_t topk,
+                       int32_t shared, void* out, uint32_t epoch, void* stream);
 int cernels_ep_status(void* ctx, int* status);
 
 /* Device status word of the last call that used this workspace (0 = ok; nonzero when a

@@ -24,7 +24,7 @@ def test_ep_wait_for_missing_dispatch_times_out_and_reports():
     H, El, F, cap = 256, 2, 128, 64
     ctx = ctypes.c_void_p()
     handle = ctypes.create_string_buffer(64)
-    _lib.check(lib.cernels_ep_create(0, 1, H, El, cap, ctypes.byref(ctx), handle), "cernels_ep_create")
+    _lib.check(lib.cernels_ep_create(0, 1, H, El, cap, 0, ctypes.byref(ctx), handle), "cernels_ep_create")
     try:
         _lib.check(lib.cernels_ep_connect(ctx, handle.raw), "cernels_ep_connect")
         w1 = torch.zeros(El, 2 * F, H, dtype=torch.bfloat16, device="cuda")
@@ -41,8 +41,8 @@ def test_ep_wait_for_missing_dispatch_times_out_and_reports():
         torch.cuda.synchronize()
         t0 = time.perf_counter()
         # epoch 7 was never dispatched: the experts step's wait for it must give up
-        _lib.check(lib.cernels_ep_experts(ctx, ctypes.byref(shape), w1.data_ptr(), None, w2.data_ptr(), None, 7,
-                                          ws.data_ptr(), n.value, stream), "cernels_ep_experts")
+        _lib.check(lib.cernels_ep_experts(ctx, ctypes.byref(shape), w1.data_ptr(), None, w2.data_ptr(), None, None,
+                                          None, 0, 7, ws.data_ptr(), n.value, stream), "cernels_ep_experts")
         torch.cuda.synchronize()
         elapsed = time.perf_counter() - t0
         _lib.check(lib.cernels_ep_status(ctx, ctypes.byref(status)), "cernels_ep_status")
