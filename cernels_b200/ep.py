@@ -198,8 +198,8 @@ class ExpertParallelMoe:
 
             from .registry import gpt_oss_moe_experts as go
 
-            def router(x):
-                return go.route(x, module)
+            def router(x, out=None):
+                return go.route(x, module, out=out)
 
             return cls(E, int(module.router.top_k), rank, world, router, backend, None, group, local_weights=local)
         if kind == "qwen3_next":
@@ -213,12 +213,12 @@ class ExpertParallelMoe:
             backend = cuda_backend(LAYOUT_LINEAR, w1, w2)
             local = (LAYOUT_LINEAR, w1, None, w2, None)
 
-            def router(x):
+            def router(x, out=None):
                 return qn.route(x, module)
 
             fused = None
             if qn.fused_shared_supported(module):
-                fused = (lambda x: qn._fused_route(x, module), qn._shared_weights(module))
+                fused = (lambda x, out=None: qn._fused_route(x, module, out=out), qn._shared_weights(module))
             return cls(E, int(module.gate.top_k), rank, world, router, backend, lambda x: qn.shared_expert(x, module),
                        group, local_weights=local, fused_shared=fused)
         raise ValueError(f"expert parallelism is not used for {kind}")
@@ -276,12 +276,17 @@ class ExpertParallelMoe:
         fused = self.fused_shared
         with torch.no_grad():
             self._mark()
-            idx, w = (fused[0] if fused is not None else self.router)(x)
-            idx = idx.to(torch.int32).contiguous()
-            w = w.float().contiguous()
+            # router outputs and routing tables live in buffers reused from step to step
+            if not hasattr(self, "_route_bufs"):
+                from . import ops
+
+                self._route_bufs = ops.RouteBuffers()
+                self._router_out = None
+            idx, w = (fused[0] if fused is not None else self.router)(x, out=self._router_out)
+            self._router_out = (idx, w)
             self._mark()
             # the shared slot's id E is outside [0, E): routing skips it (inv = -1)
-            offsets, perm_token, _perm_weight, inv = self.backend.route(idx, w, self.E)
+            offsets, perm_token, _perm_weight, inv = self.backend.route(idx, w, self.E, self._route_bufs)
             self._mark()
             if self._p2p is None:
                 # window capacity: the most routed rows (and tokens) any rank has (all ranks agree)

@@ -235,10 +235,34 @@ def run_experts_shared(x, gate_up_proj, down_proj, shared_gate_up, shared_down, 
 
 
 # ---------------------------------------------------------------- stage entry points
-def route(indices: torch.Tensor, weights: torch.Tensor, experts: int):
+class RouteBuffers:
+    """Output and scratch tensors of `route`, kept between calls of the same shape (a caller that
+    routes every step, like the expert-parallel forward, then allocates nothing per step). The
+    results of one call are overwritten by the next call on the same buffers."""
+
+    def __init__(self):
+        self._key = None
+        self._bufs = None
+
+    def get(self, T: int, k: int, experts: int, dev):
+        key = (T, k, experts, dev)
+        if key != self._key:
+            shape = _lib.MoeShape(int(T), 8, int(experts), 8, int(k), _lib.LAYOUT_LINEAR)
+            ws_bytes = _lib.workspace_bytes(shape, False)
+            self._bufs = (shape, torch.empty(experts + 1, dtype=torch.int32, device=dev),
+                          torch.zeros(T * k, dtype=torch.int32, device=dev),
+                          torch.zeros(T * k, dtype=torch.float32, device=dev),
+                          torch.empty(T * k, dtype=torch.int32, device=dev),
+                          torch.empty(ws_bytes, dtype=torch.uint8, device=dev), ws_bytes)
+            self._key = key
+        return self._bufs
+
+
+def route(indices: torch.Tensor, weights: torch.Tensor, experts: int, buffers: RouteBuffers | None = None):
     """Routing only: returns (offsets [E+1], perm_token [Tk], perm_weight [Tk], inv [Tk]).
 
-    Stable in the flat index t*topk+j; ids outside [0, E) are skipped (inv = -1).
+    Stable in the flat index t*topk+j; ids outside [0, E) are skipped (inv = -1). With `buffers`
+    the results live in (and are overwritten by the next call on) those buffers.
     """
     _check(indices.is_cuda and indices.dtype == torch.int32 and indices.is_contiguous() and indices.dim() == 2,
            "indices must be a contiguous [T, topk] int32 CUDA tensor")
@@ -246,13 +270,7 @@ def route(indices: torch.Tensor, weights: torch.Tensor, experts: int):
            "weights must be contiguous fp32 [T, topk]")
     T, k = indices.shape
     dev = indices.device
-    shape = _lib.MoeShape(int(T), 8, int(experts), 8, int(k), _lib.LAYOUT_LINEAR)
-    offsets = torch.empty(experts + 1, dtype=torch.int32, device=dev)
-    perm_token = torch.zeros(T * k, dtype=torch.int32, device=dev)
-    perm_weight = torch.zeros(T * k, dtype=torch.float32, device=dev)
-    inv = torch.empty(T * k, dtype=torch.int32, device=dev)
-    ws_bytes = _lib.workspace_bytes(shape, False)
-    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
+    shape, offsets, perm_token, perm_weight, inv, ws, ws_bytes = (buffers or RouteBuffers()).get(T, k, experts, dev)
     with torch.cuda.device(dev):
         rc = _lib.load().cernels_moe_route(ctypes.byref(shape), indices.data_ptr(), weights.data_ptr(),
                                            offsets.data_ptr(), perm_token.data_ptr(), perm_weight.data_ptr(),
@@ -316,13 +334,13 @@ def router_topk(logits: torch.Tensor, topk: int, mode: int, renorm: bool = False
 
 
 def router(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None, experts: int, topk: int, mode: int,
-           renorm: bool = False, shared_gate: bool = False, return_logits: bool = False):
+           renorm: bool = False, shared_gate: bool = False, return_logits: bool = False, out=None):
     """Fused router (cernels_router): logits = x weight^T (+ bias) on the tensor cores with the
     top-k / softmax tail in the same kernel; returns int32 ids and fp32 weights [T, topk (+1)]
     (and, with return_logits, the bf16 logits [T, weight.shape[0]] the selection used; only the
     first experts (+1) columns are written). weight: [rows >= experts (+1), H] bf16; with
     shared_gate, row `experts` is a shared expert's gate and an (experts, sigmoid(gate)) slot is
-    appended to every token."""
+    appended to every token. out: (ids, weights) tensors of that shape to write into."""
     _check(x.is_cuda and x.dim() == 2 and x.dtype == torch.bfloat16, "x must be a [T, H] bf16 CUDA tensor")
     _check(weight.is_cuda and weight.dim() == 2 and weight.dtype == torch.bfloat16 and weight.shape[1] == x.shape[1],
            "router weight must be [rows, H] bf16")
@@ -332,8 +350,11 @@ def router(x: torch.Tensor, weight: torch.Tensor, bias: torch.Tensor | None, exp
     bias = None if bias is None else bias.contiguous()
     T = x.shape[0]
     cols = topk + int(bool(shared_gate))
-    idx = torch.empty(T, cols, dtype=torch.int32, device=x.device)
-    w = torch.empty(T, cols, dtype=torch.float32, device=x.device)
+    if out is not None and tuple(out[0].shape) == (T, cols) and out[0].device == x.device:
+        idx, w = out  # reused output buffers (overwritten)
+    else:
+        idx = torch.empty(T, cols, dtype=torch.int32, device=x.device)
+        w = torch.empty(T, cols, dtype=torch.float32, device=x.device)
     logits = torch.zeros(T, weight.shape[0], dtype=torch.bfloat16, device=x.device) if return_logits else None
     with torch.cuda.device(x.device):
         rc = _lib.load().cernels_router(x.data_ptr(), T, x.shape[1], weight.data_ptr(), weight.shape[0], _ptr(bias),

@@ -22,7 +22,7 @@ def _weights(experts):
     return experts.gate_up_proj.data.contiguous(), b1, experts.down_proj.data.contiguous(), b2
 
 
-def route(xf, mlp):
+def route(xf, mlp, out=None):
     """transformers GptOssTopKRouter in one kernel (cernels_router): logits = x W^T + b on the
     tensor cores, rounded to bf16, top-k and the softmax over the k logits in its epilogue
     (int32 ids, fp32 weights)."""
@@ -32,7 +32,7 @@ def route(xf, mlp):
         logits = torch.nn.functional.linear(xf, r.weight, r.bias)
         return ops.router_topk(logits, k, ops.ROUTER_TOPK_SOFTMAX)
     return ops.router(xf, r.weight.data, None if r.bias is None else r.bias.data, int(r.weight.shape[0]), k,
-                      ops.ROUTER_TOPK_SOFTMAX)
+                      ops.ROUTER_TOPK_SOFTMAX, out=out)
 
 
 def kernel(x, mlp):

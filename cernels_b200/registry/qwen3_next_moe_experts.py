@@ -82,7 +82,7 @@ def fused_shared_supported(block) -> bool:
     return FUSE_SHARED and se.gate_proj.weight.shape[0] == block.experts.gate_up_proj.shape[1] // 2
 
 
-def _fused_route(xf, block, return_logits=False):
+def _fused_route(xf, block, return_logits=False, out=None):
     """Router + shared-expert gate in one kernel: ids / weights [T, k + 1], the last column
     (E, sigmoid(gate)); with return_logits also the bf16 logits [T, pad8(E + 1)]."""
     E = int(block.experts.gate_up_proj.shape[0])
@@ -93,7 +93,8 @@ def _fused_route(xf, block, return_logits=False):
         logits = torch.nn.functional.linear(xf, wg)
         idx, w = ops.router_topk(logits, k, ops.ROUTER_SOFTMAX_TOPK, renorm, shared_gate=E)
         return (logits, idx, w) if return_logits else (idx, w)
-    r = ops.router(xf, wg, None, E, k, ops.ROUTER_SOFTMAX_TOPK, renorm, shared_gate=True, return_logits=return_logits)
+    r = ops.router(xf, wg, None, E, k, ops.ROUTER_SOFTMAX_TOPK, renorm, shared_gate=True, return_logits=return_logits,
+                   out=out)
     return (r[2], r[0], r[1]) if return_logits else r
 
 
