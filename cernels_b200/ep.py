@@ -127,11 +127,15 @@ class P2PTransport:
         self._lib.check(lib.cernels_ep_dispatch(self.ctx, x.data_ptr(), perm_token.data_ptr(), offsets.data_ptr(),
                                                 T * k, n_shared, 0, stream), "cernels_ep_dispatch")
         mark()
-        n = ctypes.c_size_t(0)
-        self._lib.check(lib.cernels_ep_experts_workspace_bytes(self.ctx, ctypes.byref(shape), ctypes.byref(n)),
-                        "cernels_ep_experts_workspace_bytes")
-        if self._ws is None or self._ws.numel() < n.value:
-            self._ws = torch.empty(n.value, dtype=torch.uint8, device=self.device)
+        key = (shape.hidden, shape.intermediate, shape.experts, shape.layout)
+        if getattr(self, "_ws_key", None) != key:  # workspace sized once per shape
+            n = ctypes.c_size_t(0)
+            self._lib.check(lib.cernels_ep_experts_workspace_bytes(self.ctx, ctypes.byref(shape), ctypes.byref(n)),
+                            "cernels_ep_experts_workspace_bytes")
+            if self._ws is None or self._ws.numel() < n.value:
+                self._ws = torch.empty(n.value, dtype=torch.uint8, device=self.device)
+            self._ws_key = key
+        n = ctypes.c_size_t(self._ws.numel())
         sw1, sw2 = shared if shared is not None else (None, None)
         self._lib.check(lib.cernels_ep_experts(self.ctx, ctypes.byref(shape), w1.data_ptr(), ptr(b1), w2.data_ptr(),
                                                ptr(b2), ptr(sw1), ptr(sw2), n_shared, 0, self._ws.data_ptr(), n.value,
