@@ -589,6 +589,8 @@ def run_ours(args):
         elif world == 1 or cfg.name not in EP_CONFIGS:
             log("stage profile")
             roof = roofline(cfg, case, stage_profile(case, min(args.steps, 10)))
+        elif phases is not None:
+            roof = ep_roofline(cfg, world, phases)
         if world == 1 and not args.no_cpu_baseline:
             log("cpu baseline")
             cpu = cpu_oracle_baseline(case, args.cpu_sample_s)
@@ -695,6 +697,24 @@ def measure_configs(steps, device):
     out["method"] = ("CUDA events on the launch stream, 256 MB L2 flush before every timed step, "
                      f"{steps} timed steps after 3 warm-up; decode entries replayed as CUDA graphs")
     return out
+
+
+def ep_roofline(cfg, world, phases):
+    """Expert-parallel step, per rank: the grouped GEMMs' FLOPs of this rank's share of the rows
+    (total / world) over the "experts" phase (its GEMMs, plus the wait for rows still arriving),
+    against the sustained bf16 peak; with the NVLink bytes each rank sends (its routed rows that
+    leave the GPU, each way) for context."""
+    _, tf_sus, src = load_peaks(sustained=True)
+    flops = cfg.flops() / world
+    sec = phases["experts"] / 1e3
+    achieved = flops / sec / 1e12
+    row_bytes = cfg.hidden * 2
+    remote_rows = cfg.tokens * cfg.topk / world * (world - 1) / world
+    return {"bound": "tensor", "achieved": round(achieved, 1), "peak": tf_sus, "unit": "TFLOP/s",
+            "frac": round(achieved / tf_sus, 4), "kernel": "grouped GEMMs of the EP step (experts phase, per rank)",
+            "peak_source": src, "traffic": None,
+            "algorithmic": {"flops_per_rank": flops, "nvlink_bytes_per_rank_each_way": remote_rows * row_bytes},
+            "phases_ms": phases}
 
 
 def measure_ep_config(name, device, rank, world, steps, flush, dist):
