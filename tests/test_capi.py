@@ -131,3 +131,35 @@ def test_torch_ops_registered_with_reference_schemas():
         torch.empty(2, 64, 32, dtype=torch.bfloat16, device="meta"),
         torch.empty(5, 1, dtype=torch.int32, device="meta"), torch.empty(5, 1, device="meta"), 1)
     assert out.shape == (5, 64)
+
+
+def test_router_and_ep_argument_checks_before_any_launch():
+    """cernels_router / cernels_ep_* reject bad arguments with the documented codes before touching
+    the device (no GPU needed)."""
+    lib = _lib.load()
+    p = 1 << 20
+    # topk above the fused kernel's 16, topk > E, rows < E (+ gate), bad mode, H not a multiple of 8
+    assert lib.cernels_router(p, 8, 64, p, 32, None, 32, 17, 0, 0, 0, p, p, None, None) == 1
+    assert lib.cernels_router(p, 8, 64, p, 4, None, 4, 5, 0, 0, 0, p, p, None, None) == 1
+    assert lib.cernels_router(p, 8, 64, p, 32, None, 32, 4, 0, 0, 1, p, p, None, None) == 1
+    assert lib.cernels_router(p, 8, 64, p, 32, None, 32, 4, 9, 0, 0, p, p, None, None) == 1
+    assert lib.cernels_router(p, 8, 60, p, 32, None, 32, 4, 0, 0, 0, p, p, None, None) == 2
+    # empty batch: nothing to do; NULL outputs
+    assert lib.cernels_router(None, 0, 64, None, 32, None, 32, 4, 0, 0, 0, None, None, None, None) == 0
+    assert lib.cernels_router(p, 8, 64, p, 32, None, 32, 4, 0, 0, 0, None, p, None, None) == 6
+    # misaligned x
+    assert lib.cernels_router(p + 4, 8, 64, p, 32, None, 32, 4, 0, 0, 0, p, p, None, None) == 2
+    # EP: world / rank / sizes / shared rows
+    ctx = ctypes.c_void_p()
+    h = ctypes.create_string_buffer(64)
+    assert lib.cernels_ep_create(0, 0, 64, 4, 16, 0, ctypes.byref(ctx), h) == 1
+    assert lib.cernels_ep_create(2, 2, 64, 4, 16, 0, ctypes.byref(ctx), h) == 1
+    assert lib.cernels_ep_create(0, 2, 60, 4, 16, 0, ctypes.byref(ctx), h) == 1
+    assert lib.cernels_ep_create(0, 2, 64, 4, 16, -1, ctypes.byref(ctx), h) == 1
+    assert lib.cernels_ep_create(0, 16, 64, 256, 16, 0, ctypes.byref(ctx), h) == 5  # 4096 experts
+    # a NULL / unconnected context
+    assert lib.cernels_ep_dispatch(None, p, p, p, 4, 0, 0, None) == 6
+    assert lib.cernels_ep_combine(None, p, p, 4, 2, 0, p, 0, None) == 6
+    # the wait limit is a plain setting
+    assert lib.cernels_set_wait_limit_ns(1_000_000) == 0
+    assert lib.cernels_set_wait_limit_ns(0) == 0
