@@ -788,9 +788,9 @@ __device__ __forceinline__ UnitCoord unit_coord(const StreamShared& S, int u, in
 //            weight stages, which do not depend on phase 1
 //            (and, when they fit in L2, has prefetched its share of them into L2)
 //   phase 2  units (group, token batch, r2 down rows); the batch's fp32 glu rows sit in a
-//            per-CTA buffer reloaded when the unit's (group, batch) changes -> partial[pair, h];
-//            the last unit to finish a row chunk (arrival counter) writes
-//            out[t, h] = bf16(sum_j w[t, j] * partial[(t, j), h]) for it, in slot order j
+//            per-CTA buffer reloaded when the unit's (group, batch) changes -> partial[pair, h]
+//   barrier  (bounded, grid-wide), then every CTA combines a share of the output rows:
+//            out[t, h] = bf16(sum_j w[t, j] * partial[(t, j), h]) in slot order j
 // Every stage is split over all 256 consumer threads by columns (each thread owns 16-byte
 // vectors of every row in the stage), then reduced per row with shuffles + shared memory.
 __global__ void __launch_bounds__(kStreamThreads, 1) decode_stream_linear(
@@ -810,7 +810,6 @@ __global__ void __launch_bounds__(kStreamThreads, 1) decode_stream_linear(
   const int hv = H / 8, fv = F / 8;
   const StreamPlan plan = make_stream_plan(H, F);
   volatile int* abort_flag = &S.abort;
-  int* chunk_count = reinterpret_cast<int*>(barrier + 2);  // [nhr] arrivals per down-row chunk
   DECODE_TRACE(0);
 
   if (threadIdx.x == 0) {
@@ -1029,37 +1028,42 @@ __global__ void __launch_bounds__(kStreamThreads, 1) decode_stream_linear(
         }
         consumers_sync();
       }
-      // Arrival on this row chunk; the last of its n_batches units writes the output rows
-      // (sum over slots j = 0..topk-1 in order, independent of arrival order).
-      const int hr = c.r0 / plan.r2;
-      __threadfence();
-      consumers_sync();
-      if (threadIdx.x == 0) G.flag = atomicAdd(&chunk_count[hr], 1) == n_batches - 1;
-      consumers_sync();
-      if (G.flag) {
-        __threadfence();
-        for (int i = threadIdx.x; i < tokens * c.rows; i += kStreamCThreads) {
-          const int t = i / c.rows, h = c.r0 + (i - t * c.rows);
-          float acc = 0.f;
-          for (int j = 0; j < topk; ++j) {
-            const int p = t * topk + j;
-            const int e = indices[p];
-            if (e < 0 || e >= experts) continue;
-            acc = fmaf(weights[p], __ldcg(partial + static_cast<size_t>(p) * H + h), acc);
-          }
-          out[static_cast<size_t>(t) * H + h] = __float2bfloat16_rn(acc);
-        }
-      }
       __syncwarp();
       if (lane == 0) mbar_arrive(&S.empty[stage]);
       advance();
     }
     DECODE_TRACE(4);
   }
-  // no group at all: every output row is zero
-  if (n_groups == 0)
-    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < tokens * H; i += gridDim.x * blockDim.x)
-      out[i] = __float2bfloat16_rn(0.f);
+  // Every partial row is written: one more grid barrier, then all CTAs combine the output rows,
+  // out[t, h] = bf16(sum_j w[t, j] * partial[(t, j), h]) over valid slots in order j = 0..topk-1
+  // (zero rows when no slot is valid). One grid barrier costs less than a last-arriver combine
+  // per phase-2 unit (a fence, an atomic and two CTA-wide syncs for every unit).
+  if (!grid_barrier_bounded(barrier, gridDim.x, status, kStatusTimeoutOther, &G.flag, wait_ns)) {
+    if (warp == kStreamConsumers && lane == 0) drain();
+    return;
+  }
+  DECODE_TRACE(5);
+  const int h4 = H / 4;
+  for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < tokens * h4; i += gridDim.x * blockDim.x) {
+    const int t = i / h4, q = i - t * h4;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int j = 0; j < topk; ++j) {
+      const int p = t * topk + j;
+      const int e = indices[p];
+      if (e < 0 || e >= experts) continue;
+      const float w = weights[p];
+      const float4 v = __ldcg(reinterpret_cast<const float4*>(partial + static_cast<size_t>(p) * H) + q);
+      acc.x = fmaf(w, v.x, acc.x);
+      acc.y = fmaf(w, v.y, acc.y);
+      acc.z = fmaf(w, v.z, acc.z);
+      acc.w = fmaf(w, v.w, acc.w);
+    }
+    __nv_bfloat162 lo = __floats2bfloat162_rn(acc.x, acc.y), hi = __floats2bfloat162_rn(acc.z, acc.w);
+    uint2 packed;
+    packed.x = *reinterpret_cast<uint32_t*>(&lo);
+    packed.y = *reinterpret_cast<uint32_t*>(&hi);
+    *reinterpret_cast<uint2*>(out + static_cast<size_t>(t) * H + 4 * q) = packed;
+  }
   DECODE_TRACE(6);
 }
 
@@ -1137,8 +1141,8 @@ cudaError_t launch_decode(const DecodeArgs& a, const DecodeWorkspace& ws, cudaSt
       const int units = max_groups * std::max(plan.nfr, plan.nhr);
       int grid = std::min(per_sm * device_sm_count(), units);
       if (grid < 1) grid = 1;
-      // grid barrier words and the per-chunk arrival counters start at zero
-      if ((err = cudaMemsetAsync(ws.counters, 0, (2 + plan.nhr) * sizeof(int), stream)) != cudaSuccess) return err;
+      // the grid barrier's words start at zero
+      if ((err = cudaMemsetAsync(ws.counters, 0, 2 * sizeof(int), stream)) != cudaSuccess) return err;
       cudaLaunchConfig_t cfg = {};
       cfg.gridDim = dim3(grid);
       cfg.blockDim = dim3(kStreamThreads);
@@ -1191,3 +1195,9 @@ cudaError_t launch_decode(const DecodeArgs& a, const DecodeWorkspace& ws, cudaSt
 size_t decode_counter_count(int hidden) { return static_cast<size_t>(hidden / 16 + 1); }
 
 }  // namespace cernels
+
+#ifdef CERNELS_DECODE_TRACE
+extern "C" int cernels_debug_decode_trace(unsigned long long* host, int rows) {
+  return cudaMemcpyFromSymbol(host, cernels::g_decode_trace, sizeof(unsigned long long) * 8 * rows) == cudaSuccess ? 0 : 4;
+}
+#endif
