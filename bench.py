@@ -237,7 +237,7 @@ def time_device(step, inputs, steps, warmup, flush, graph=False, align=None):
     return total_ms, per
 
 
-def time_e2e(step, inputs, steps, warmup, flush, chunks=1):
+def time_e2e(step, inputs, steps, warmup, flush, chunks=1, taper=False):
     """Pinned host inputs -> device -> step -> host output, per step, CUDA events. With
     chunks > 1 the public HostPipeline overlaps the copies of one token chunk with the compute
     of another (the result is identical: tokens are independent)."""
@@ -254,7 +254,7 @@ def time_e2e(step, inputs, steps, warmup, flush, chunks=1):
     pipe = HostPipeline()
 
     def one():
-        pipe.run(step, host_in, host_out, chunks)
+        pipe.run(step, host_in, host_out, chunks, taper)
 
     for _ in range(warmup):
         one()
@@ -535,12 +535,13 @@ def run_ours(args):
         total_ms = float(t.item())
         dist.barrier()
     # token-chunked copy/compute overlap for large single-GPU batches (EP steps are collective)
-    # token chunks of the host pipeline: tried 4 and 8 for large single-GPU batches, the faster kept
-    chunk_options = (4, 8) if (world == 1 and cfg.tokens >= 4096) else (1,)
+    # token chunks of the host pipeline: for large single-GPU batches 4 and 8 equal chunks and 4
+    # tapered ones (half-size first and last) are tried, the fastest kept
+    chunk_options = ((4, False), (8, False), (4, True)) if (world == 1 and cfg.tokens >= 4096) else ((1, False),)
     log("e2e")
     e2e_tried = {}
-    for ch in chunk_options:
-        e2e_tried[ch] = time_e2e(step, inputs, args.steps, warmup, flush, ch)
+    for ch, taper in chunk_options:
+        e2e_tried[f"{ch}{'t' if taper else ''}"] = time_e2e(step, inputs, args.steps, warmup, flush, ch, taper)
     e2e_chunks = min(e2e_tried, key=lambda ch: e2e_tried[ch][0])
     e2e_ms, h2d, d2h = e2e_tried[e2e_chunks]
     if world > 1:
@@ -612,7 +613,7 @@ def run_ours(args):
             "roofline": roof, "cpu_baseline": cpu,
             "e2e": {"value": round(e2e_value, 1), "unit": "tokens/s", "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h, "token_chunks": e2e_chunks,
-                    "chunk_options_ms_per_step": {str(ch): round(v[0] / args.steps, 4) for ch, v in e2e_tried.items()}},
+                    "chunk_options_ms_per_step": {ch: round(v[0] / args.steps, 4) for ch, v in e2e_tried.items()}},
             "hot_l2": hot,
             "gpu_launches": launches * args.steps,
             "clocks": clocks.summary(),

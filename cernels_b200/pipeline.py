@@ -30,12 +30,27 @@ class HostPipeline:
             self._bufs[key] = b
         return b
 
-    def run(self, step: Callable, host_inputs: list[torch.Tensor], out_host: torch.Tensor, chunks: int = 4):
+    @staticmethod
+    def chunk_bounds(T: int, chunks: int, taper: bool = False) -> list[int]:
+        """Token boundaries of the chunks. With taper, the first and last chunks are half the size
+        of the others, so the pipeline fills (first copy in) and drains (last copy out) faster."""
+        chunks = max(1, min(int(chunks), T))
+        if not taper or chunks < 3:
+            return [(T * c) // chunks for c in range(chunks + 1)]
+        units = 2 * chunks - 2  # half-size first and last chunks, full-size (2 units) middle ones
+        edges = [0, 1] + [1 + 2 * c for c in range(1, chunks - 1)] + [units]
+        bounds = [(T * e) // units for e in edges]
+        if any(b <= a for a, b in zip(bounds[:-1], bounds[1:])):  # too few tokens: equal chunks
+            return [(T * c) // chunks for c in range(chunks + 1)]
+        return bounds
+
+    def run(self, step: Callable, host_inputs: list[torch.Tensor], out_host: torch.Tensor, chunks: int = 4,
+            taper: bool = False):
         """step(*device_chunks) -> device output rows for those tokens. host_inputs are pinned
         [T, ...] tensors split along dim 0; out_host is a pinned [T, ...] tensor, written."""
         T = host_inputs[0].shape[0]
-        chunks = max(1, min(int(chunks), T))
-        bounds = [(T * c) // chunks for c in range(chunks + 1)]
+        bounds = self.chunk_bounds(T, chunks, taper)
+        chunks = len(bounds) - 1
         dev_in = [self._buffer(("in", i), t) for i, t in enumerate(host_inputs)]
         compute = torch.cuda.current_stream(self.device)
         self.copy_in.wait_stream(compute)   # buffers are free once earlier work finished
