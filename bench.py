@@ -194,9 +194,11 @@ def make_step(cfg, case, kind, module, world, rank):
 
 
 def time_device(step, inputs, steps, warmup, flush, graph=False, align=None):
-    """CUDA-event time of `steps` calls (ms total, per-step list). `align` (multi-GPU) runs
-    before each step, outside its timed interval, so that every rank starts the step together
-    and a step's time does not include another rank's late start."""
+    """CUDA-event time of `steps` calls (ms total, per-step list): events on the launch stream
+    around each step, the L2 flush between steps outside them, one synchronisation after the last
+    step (the host enqueues ahead, as a serving loop does, so Python launch overhead stays off the
+    device timeline). `align` (multi-GPU) runs before each step, outside its timed interval, so
+    that every rank starts the step together; it synchronises the host every step."""
     import torch
 
     stream = torch.cuda.current_stream()
@@ -215,8 +217,7 @@ def time_device(step, inputs, steps, warmup, flush, graph=False, align=None):
         with torch.cuda.graph(g):
             step(*inputs)
         torch.cuda.synchronize()
-    total_ms = 0.0
-    per = []
+    marks = []
     for _ in range(steps):
         if flush is not None:
             flush.zero_()
@@ -230,11 +231,10 @@ def time_device(step, inputs, steps, warmup, flush, graph=False, align=None):
         else:
             step(*inputs)
         b.record(stream)
-        b.synchronize()
-        ms = a.elapsed_time(b)
-        per.append(ms)
-        total_ms += ms
-    return total_ms, per
+        marks.append((a, b))
+    torch.cuda.synchronize()
+    per = [a.elapsed_time(b) for a, b in marks]
+    return sum(per), per
 
 
 def time_e2e(step, inputs, steps, warmup, flush, chunks=1, taper=False):
@@ -562,12 +562,13 @@ def run_ours(args):
         # per-phase device times of the EP step (CUDA events between the phases' launches, L2
         # flushed before each step), median over steps, max over ranks
         planner = step.planner
-        rows = []
-        for _ in range(max(3, min(args.steps, 10))):
+        kept = []
+        for _ in range(max(3, min(args.steps, 10))):  # no host sync between steps (as in the timed loop)
             flush.zero_()
             planner.timing = []
             step(*inputs)
-            rows.append(planner.phase_ms())
+            kept.append(planner.timing)
+        rows = [planner.phase_ms(ev) for ev in kept]
         planner.timing = None
         names = list(rows[0].keys())
         med = torch.tensor([statistics.median(r[n] for r in rows) for n in names], device=device)
@@ -736,12 +737,13 @@ def measure_ep_config(name, device, rank, world, steps, flush, dist):
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
         ms = float(t.item()) / steps
         planner = step.planner
-        rows = []
-        for _ in range(3):
+        kept = []
+        for _ in range(3):  # no host sync between steps (as in the timed loop)
             flush.zero_()
             planner.timing = []
             step(*inputs)
-            rows.append(planner.phase_ms())
+            kept.append(planner.timing)
+        rows = [planner.phase_ms(ev) for ev in kept]
         planner.timing = None
         names = list(rows[0].keys())
         med = torch.tensor([statistics.median(r[n] for r in rows) for n in names], device=device)

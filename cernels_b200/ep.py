@@ -264,10 +264,11 @@ class ExpertParallelMoe:
             ev.record()
             self.timing.append(ev)
 
-    def phase_ms(self):
-        """Per-phase device times (ms) of the last timed forward (PHASES order; the shared
-        expert's phase is 0 when there is none). Synchronises."""
-        ev = self.timing
+    def phase_ms(self, events=None):
+        """Per-phase device times (ms) of the last timed forward, or of the event list `events` kept
+        from an earlier one (PHASES order; the shared expert's phase is 0 when there is none).
+        Synchronises."""
+        ev = self.timing if events is None else events
         torch.cuda.synchronize()
         out = [a.elapsed_time(b) for a, b in zip(ev[:-1], ev[1:])]
         return dict(zip(self.PHASES, out + [0.0] * (len(self.PHASES) - len(out))))
