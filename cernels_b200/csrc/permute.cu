@@ -26,7 +26,20 @@ __global__ void __launch_bounds__(kRowThreads) gather_rows_kernel(const uint4* _
   const int t = perm_token[row];
   const uint4* src = x + static_cast<size_t>(t) * vec_per_row;
   uint4* dst = out + static_cast<size_t>(row) * vec_per_row;
-  for (int v = lane; v < vec_per_row; v += 32) dst[v] = src[v];
+  // up to 8 loads per lane in flight before their stores
+  for (int v0 = 0; v0 < vec_per_row; v0 += 32 * 8) {
+    uint4 r[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int v = v0 + j * 32 + lane;
+      if (v < vec_per_row) r[j] = src[v];
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const int v = v0 + j * 32 + lane;
+      if (v < vec_per_row) dst[v] = r[j];
+    }
+  }
 }
 
 __device__ __forceinline__ void accumulate_bf16x8(float (&acc)[8], const uint4& v, float w) {
